@@ -1,0 +1,139 @@
+/*
+ * nsa_sel.h -- C ABI of the B200 (sm_100a) NSA selected-branch attention forward.
+ *
+ * This is the drop-in boundary for the one hot path of the nsa-hopper reference: the
+ * selected-branch forward that its kernels expose through pybind as
+ *
+ *     torch::Tensor forward(Tensor Q, Tensor K, Tensor V, Tensor sel,
+ *                           int64 l_prime, int64 BQ, Tensor cyc)
+ *
+ * (reference nsa_v0.cu:118-146, nsa_v1.cu:125-147, nsa_v2.cu:147-170).  Every entry point
+ * takes plain pointers and sizes; no torch type crosses this boundary.  The library never
+ * allocates device memory: all buffers belong to the caller.  All launches go to the stream
+ * passed in; a call returns as soon as the work is queued (like the reference op, which is
+ * asynchronous on the legacy stream).  The library is reentrant: concurrent calls from
+ * several host threads are safe; the error text is kept per host thread.
+ *
+ * Layouts (all contiguous, row-major, as in the reference):
+ *   Q   bf16 [B, Hq,  T, d_qk]        K bf16 [B, Hkv, T, d_qk]      V bf16 [B, Hkv, T, d_v]
+ *   sel int32 [B, Hkv, NQB, KSEL]    NQB = ceil(T / BQ); entry = block index (block = l_prime
+ *                                     keys); negative entries are padding and are skipped
+ *   O   [B, Hq, T, d_v]  bf16 or fp32 (every element is written; rows with no visible key = 0)
+ *   LSE fp32 [B, Hq, T]  natural log of sum_j exp(scale * q.k_j) over the visible keys
+ *                        (-inf for a row with no visible key)
+ *   cyc int64 [NQB * B * Hkv * 2]  optional; slot (b*Hkv+kvh)*NQB+qb holds
+ *                        {cycles the MMA issuer waited for K/V tiles, other cycles}
+ *
+ * Semantics (pinned against the reference's PyTorch oracle ref_only.py:2-20 and
+ * nsa_reference.py:18-25,66-77): query token t of KV head kvh attends to every key position
+ * p with p <= t inside the selected blocks of its query block; selection is a set
+ * (duplicates count once); entries < 0 or >= ceil(T / l_prime) select nothing; the softmax
+ * scale defaults to 1/sqrt(d_qk); a row with no visible key gives O = 0.
+ */
+#ifndef NSA_SEL_H_
+#define NSA_SEL_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same object as cudaStream_t; NULL is the legacy default stream. */
+typedef struct CUstream_st* nsa_stream_t;
+
+#define NSA_SEL_VERSION 10000 /* 1.0.0 */
+
+/* Return codes (0 = success). */
+#define NSA_OK 0
+#define NSA_ERR_INVALID_ARG (-1) /* bad pointer, shape, stride or alignment */
+#define NSA_ERR_UNSUPPORTED (-2) /* valid request outside the built kernel family */
+#define NSA_ERR_CUDA (-3)        /* a CUDA runtime call failed; see nsa_sel_last_error() */
+#define NSA_ERR_DRIVER (-4)      /* the driver entry point for tensor maps is unavailable */
+
+/* Bits a kernel ORs into the optional device error word (nsa_sel_desc.err). */
+#define NSA_DEVERR_TIMEOUT 1 /* a bounded wait inside the kernel ran out; outputs invalid */
+
+/* Test hook: the MMA warp starts with a wait that nothing completes, so the launch ends through
+   the bounded-wait error path (NSA_DEVERR_TIMEOUT after timeout_ms) without any fault. */
+#define NSA_DEBUG_STALL 1
+
+#define NSA_DTYPE_BF16 0
+#define NSA_DTYPE_F32 1
+
+/* Full description of one call.  Zero-initialise, then fill the fields you need. */
+typedef struct nsa_sel_desc {
+  const void* q;              /* bf16 [B, Hq, T, d_qk] */
+  const void* k;              /* bf16 [B, Hkv, T, d_qk] */
+  const void* v;              /* bf16 [B, Hkv, T, d_v] */
+  const int32_t* sel;         /* int32 [B, Hkv, NQB, KSEL] */
+  const int32_t* cu_seqlens;  /* optional int32 [n_seqs + 1]: packed varlen batch (B == 1, BQ == 1);
+                                 block ids are relative to each sequence's first token */
+  void* o;                    /* [B, Hq, T, d_v], dtype o_dtype */
+  float* lse;                 /* optional fp32 [B, Hq, T] */
+  int64_t* cyc;               /* optional int64 [NQB * B * Hkv * 2], accumulated into */
+  int32_t* err;               /* optional device int32; NSA_DEVERR_* bits are ORed into it */
+  int32_t batch, heads_q, heads_kv, seq_len, d_qk, d_v;
+  int32_t n_qblocks;          /* NQB, must equal ceil(seq_len / q_block) */
+  int32_t n_sel;              /* KSEL */
+  int32_t block_size;         /* l_prime: 64, 128 or 256 */
+  int32_t q_block;            /* BQ: query tokens sharing one selection row (1 = per token) */
+  int32_t n_seqs;             /* number of sequences when cu_seqlens is set */
+  int32_t o_dtype;            /* NSA_DTYPE_BF16 or NSA_DTYPE_F32 */
+  float scale;                /* softmax scale; <= 0 selects 1/sqrt(d_qk) */
+  /* Shard: process only (b*Hkv+kvh) in [bkv_begin, bkv_end) and query blocks in
+     [qb_begin, qb_end); an end of 0 means "to the end".  Outputs outside the shard are
+     left untouched. */
+  int32_t bkv_begin, bkv_end, qb_begin, qb_end;
+  int32_t timeout_ms;         /* bound on every in-kernel wait; 0 = default (2000 ms) */
+  int32_t max_ctas;           /* 0 = one CTA per SM */
+  int32_t debug_flags;        /* NSA_DEBUG_* bits; 0 in normal use */
+  int32_t reserved[5];
+} nsa_sel_desc;
+
+/* Launch plan chosen for a description (filled by nsa_sel_plan, used by the launcher). */
+typedef struct nsa_sel_plan_info {
+  int32_t n_cols;       /* N of the tensor-core tiles: G * q_tokens_per_unit rounded up */
+  int32_t q_per_unit;   /* query tokens per work unit */
+  int32_t parts;        /* work units per query block */
+  int32_t n_units;      /* work units in the shard */
+  int32_t k_stages, v_stages;
+  int32_t smem_bytes;
+  int32_t grid;
+  int32_t tmem_cols;
+  int32_t reserved[7];
+} nsa_sel_plan_info;
+
+/* Replaces the reference's forward(Q,K,V,sel,l_prime,BQ,cyc) (nsa_v2.cu:147-170,
+   nsa_v1.cu:125-147, nsa_v0.cu:118-146): fp32 O, d_qk == d_v == D, scale 1/sqrt(D).
+   cyc may be NULL (the reference passes an empty tensor for "none", nsa_v2.cu:159). */
+int nsa_sel_forward(const void* q, const void* k, const void* v, const int32_t* sel, float* o, int64_t* cyc,
+                    int32_t B, int32_t Hq, int32_t Hkv, int32_t S, int32_t D, int32_t NQB, int32_t KSEL,
+                    int32_t l_prime, int32_t BQ, nsa_stream_t stream);
+
+/* The BASELINE path: bf16 O plus fp32 LSE, d_qk may differ from d_v, optional varlen.
+   Extends the same reference op (nsa_v2.cu:147) with the outputs the reference lacks. */
+int nsa_sel_forward_lse(const void* q, const void* k, const void* v, const int32_t* sel,
+                        const int32_t* cu_seqlens, int32_t n_seqs, void* o, float* lse, int32_t o_dtype,
+                        int32_t B, int32_t Hq, int32_t Hkv, int32_t T, int32_t d_qk, int32_t d_v, int32_t NQB,
+                        int32_t KSEL, int32_t l_prime, int32_t BQ, float scale, nsa_stream_t stream);
+
+/* General entry point: everything above plus shards, cycle counters, a device error word
+   and the wait bound.  Same reference op (nsa_v2.cu:147-170). */
+int nsa_sel_run(const nsa_sel_desc* desc, nsa_stream_t stream);
+
+/* Validate a description and report the launch plan without touching the GPU.
+   sm_count <= 0 means "query the current device". */
+int nsa_sel_plan(const nsa_sel_desc* desc, int32_t sm_count, nsa_sel_plan_info* out);
+
+/* Text of the last error on this host thread ("" if none). */
+const char* nsa_sel_last_error(void);
+
+/* NSA_SEL_VERSION of the loaded library. */
+int32_t nsa_sel_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NSA_SEL_H_ */

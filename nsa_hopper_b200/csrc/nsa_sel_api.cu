@@ -1,0 +1,475 @@
+// Host side of the C ABI declared in include/nsa_sel.h: argument validation, launch
+// planning (work-unit split, tensor-core N, ring depths within the 227 KB shared-memory
+// budget), TMA tensor-map encoding and dispatch over the compiled kernel family.
+//
+// Boundary being replaced: the reference's libtorch op `forward(Q,K,V,sel,l_prime,BQ,cyc)`
+// (nsa_v2.cu:147-170; same op in nsa_v1.cu:125-147 and nsa_v0.cu:118-146), which reads shapes
+// from tensors, allocates a zeroed fp32 O, sets scale = 1/sqrt(D) and launches one CTA per
+// (query block, b*Hkv) on the legacy stream.  This launcher takes caller-owned buffers, runs
+// on the stream it is given and launches one persistent CTA per SM.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <math.h>
+#include <mutex>
+#include <stdarg.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "nsa_sel.h"
+#include "nsa_sel_kernel.cuh"
+
+namespace {
+
+thread_local char g_last_error[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(NSA_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+constexpr int kSmemLimit = 232448;  // 227 KB opt-in dynamic shared memory per block on sm_100
+constexpr int kMaxCols = 64;        // widest N of the tensor-core tiles (G * tokens per unit)
+constexpr int kMaxSub = 128;        // widest per-unit list of 64-key sub-blocks
+constexpr int kMaxDevices = 64;
+
+// ------------------------------------------------------------------ driver entry point
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  return g_encode;
+}
+
+// ------------------------------------------------------------------ per-device cache
+struct DeviceCache {
+  std::mutex mu;
+  int sm_count[kMaxDevices] = {};
+  uint64_t attr_done[kMaxDevices] = {};  // one bit per kernel instantiation
+};
+DeviceCache g_dev;
+
+int current_sm_count(int* sm_count, int* device) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(NSA_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_dev.mu);
+  if (g_dev.sm_count[dev] == 0) {
+    int n = 0;
+    e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(SM count)");
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    if (major != 10 || minor != 0)
+      return fail(NSA_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a (B200)", dev, major,
+                  minor);
+    g_dev.sm_count[dev] = n;
+  }
+  *sm_count = g_dev.sm_count[dev];
+  *device = dev;
+  return NSA_OK;
+}
+
+// ------------------------------------------------------------------ kernel family
+using bf16 = __nv_bfloat16;
+
+typedef void (*KernelFn)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap,
+                         const nsa::Params);
+typedef nsa::SmemLayout (*LayoutFn)(int, int, int, int);
+
+struct Variant {
+  int dqk, dv, ncol, out_f32;
+  KernelFn kernel;
+  LayoutFn layout;
+  int k_stage, v_stage, tmem_cols;
+};
+
+template <int DQK, int DV, int NCOL, typename OutT>
+Variant make_variant() {
+  using C = nsa::Cfg<DQK, DV, NCOL, OutT>;
+  return Variant{DQK,
+                 DV,
+                 NCOL,
+                 sizeof(OutT) == 4 ? 1 : 0,
+                 reinterpret_cast<KernelFn>(&nsa::nsa_sel_fwd_kernel<C>),
+                 &nsa::smem_layout<C>,
+                 C::kKStage,
+                 C::kVStage,
+                 C::kTmemCols};
+}
+
+#define NSA_VARIANTS_FOR(DQK, DV)                                                                         \
+  make_variant<DQK, DV, 16, bf16>(), make_variant<DQK, DV, 32, bf16>(), make_variant<DQK, DV, 64, bf16>(), \
+      make_variant<DQK, DV, 16, float>(), make_variant<DQK, DV, 32, float>(), make_variant<DQK, DV, 64, float>()
+
+const Variant* variants(int* n) {
+  static const Variant v[] = {NSA_VARIANTS_FOR(64, 64), NSA_VARIANTS_FOR(128, 128), NSA_VARIANTS_FOR(192, 128)};
+  *n = (int)(sizeof(v) / sizeof(v[0]));
+  return v;
+}
+
+int find_variant(int dqk, int dv, int ncol, int out_f32) {
+  int n = 0;
+  const Variant* v = variants(&n);
+  for (int i = 0; i < n; ++i)
+    if (v[i].dqk == dqk && v[i].dv == dv && v[i].ncol == ncol && v[i].out_f32 == out_f32) return i;
+  return -1;
+}
+
+// ------------------------------------------------------------------ planning
+struct Plan {
+  int G, BQs, parts, ncol, maxsub, n_units, KS, VS, alias, grid, variant;
+  int bkv_begin, bkv_end, qb_begin, qb_end;
+  nsa::SmemLayout layout;
+};
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int make_plan(const nsa_sel_desc* d, int sm_count, Plan* pl) {
+  if (d == nullptr) return fail(NSA_ERR_INVALID_ARG, "desc is NULL");
+  if (d->q == nullptr || d->k == nullptr || d->v == nullptr || d->sel == nullptr || d->o == nullptr)
+    return fail(NSA_ERR_INVALID_ARG, "q, k, v, sel and o must be non-NULL");
+  if (!aligned16(d->q) || !aligned16(d->k) || !aligned16(d->v) || !aligned16(d->o))
+    return fail(NSA_ERR_INVALID_ARG, "q, k, v and o must be 16-byte aligned (TMA requirement)");
+  if ((reinterpret_cast<uintptr_t>(d->sel) & 3u) != 0) return fail(NSA_ERR_INVALID_ARG, "sel must be 4-byte aligned");
+  const int B = d->batch, Hq = d->heads_q, Hkv = d->heads_kv, T = d->seq_len;
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || T <= 0) return fail(NSA_ERR_INVALID_ARG, "B, Hq, Hkv, T must be positive");
+  if (Hq % Hkv != 0) return fail(NSA_ERR_INVALID_ARG, "Hq (%d) must be a multiple of Hkv (%d)", Hq, Hkv);
+  const int G = Hq / Hkv;
+  if (G > kMaxCols) return fail(NSA_ERR_UNSUPPORTED, "group size G=%d exceeds %d", G, kMaxCols);
+  if (d->d_qk <= 0 || d->d_v <= 0) return fail(NSA_ERR_INVALID_ARG, "d_qk and d_v must be positive");
+  if (d->block_size <= 0) return fail(NSA_ERR_INVALID_ARG, "l_prime must be positive");
+  if (d->block_size % 64 != 0 || d->block_size > 256)
+    return fail(NSA_ERR_UNSUPPORTED, "l_prime=%d: the kernel family supports 64, 128 and 256", d->block_size);
+  if (d->q_block <= 0) return fail(NSA_ERR_INVALID_ARG, "BQ must be positive");
+  const int NQB = (T + d->q_block - 1) / d->q_block;
+  if (d->n_qblocks != NQB)
+    return fail(NSA_ERR_INVALID_ARG, "sel has NQB=%d query blocks, expected ceil(T/BQ)=%d", d->n_qblocks, NQB);
+  if (d->n_sel <= 0) return fail(NSA_ERR_INVALID_ARG, "KSEL must be positive");
+  const int spb = d->block_size / 64;
+  if ((long long)d->n_sel * spb > kMaxSub)
+    return fail(NSA_ERR_UNSUPPORTED, "KSEL*l_prime/64 = %lld exceeds %d sub-blocks", (long long)d->n_sel * spb,
+                kMaxSub);
+  if (d->o_dtype != NSA_DTYPE_BF16 && d->o_dtype != NSA_DTYPE_F32)
+    return fail(NSA_ERR_INVALID_ARG, "o_dtype must be NSA_DTYPE_BF16 or NSA_DTYPE_F32");
+  if (d->cu_seqlens != nullptr) {
+    if (B != 1) return fail(NSA_ERR_INVALID_ARG, "a varlen batch (cu_seqlens) needs B == 1");
+    if (d->q_block != 1) return fail(NSA_ERR_UNSUPPORTED, "a varlen batch needs per-token selection (BQ == 1)");
+    if (d->n_seqs <= 0) return fail(NSA_ERR_INVALID_ARG, "n_seqs must be positive with cu_seqlens");
+  }
+  // 32-bit coordinates and index arithmetic inside the kernel.
+  if ((long long)T * d->d_qk >= (1ll << 31) || (long long)B * Hkv * NQB * d->n_sel >= (1ll << 31))
+    return fail(NSA_ERR_UNSUPPORTED, "problem too large for 32-bit coordinates");
+
+  // Tokens per work unit: the largest divisor of BQ with G * tokens <= 128.
+  int bqs = 1;
+  for (int c = d->q_block; c >= 1; --c)
+    if (d->q_block % c == 0 && G * c <= kMaxCols) { bqs = c; break; }
+  const int rows = G * bqs;
+  int ncol = 16;
+  while (ncol < rows) ncol <<= 1;
+  const int vi = find_variant(d->d_qk, d->d_v, ncol, d->o_dtype == NSA_DTYPE_F32 ? 1 : 0);
+  if (vi < 0)
+    return fail(NSA_ERR_UNSUPPORTED, "no kernel for (d_qk=%d, d_v=%d); built: (64,64), (128,128), (192,128)",
+                d->d_qk, d->d_v);
+  int nv = 0;
+  const Variant& V = variants(&nv)[vi];
+
+  pl->G = G;
+  pl->BQs = bqs;
+  pl->parts = d->q_block / bqs;
+  pl->ncol = ncol;
+  pl->maxsub = d->n_sel * spb;
+  pl->variant = vi;
+  pl->bkv_begin = d->bkv_begin;
+  pl->bkv_end = d->bkv_end > 0 ? d->bkv_end : B * Hkv;
+  pl->qb_begin = d->qb_begin;
+  pl->qb_end = d->qb_end > 0 ? d->qb_end : NQB;
+  if (pl->bkv_begin < 0 || pl->bkv_begin >= pl->bkv_end || pl->bkv_end > B * Hkv)
+    return fail(NSA_ERR_INVALID_ARG, "shard bkv range [%d,%d) invalid for B*Hkv=%d", pl->bkv_begin, pl->bkv_end,
+                B * Hkv);
+  if (pl->qb_begin < 0 || pl->qb_begin >= pl->qb_end || pl->qb_end > NQB)
+    return fail(NSA_ERR_INVALID_ARG, "shard query-block range [%d,%d) invalid for NQB=%d", pl->qb_begin,
+                pl->qb_end, NQB);
+  const long long units = (long long)(pl->bkv_end - pl->bkv_begin) * (pl->qb_end - pl->qb_begin) * pl->parts;
+  if (units >= (1ll << 31)) return fail(NSA_ERR_UNSUPPORTED, "too many work units");
+  pl->n_units = (int)units;
+
+  // Ring depths: the deepest equal K/V rings that fit, then one more K stage if it fits.  The
+  // output staging tile gets its own double buffer unless aliasing it into the transpose
+  // buffer buys a deeper ring (wide tiles).
+  auto fits = [&](int k, int v, int a) { return (int)V.layout(k, v, pl->maxsub, a).total <= kSmemLimit; };
+  int ks = 0, vs = 0, alias = 0;
+  for (int a = 0; a <= 1; ++a) {
+    int s = 0;
+    for (int c = nsa::kMaxStages; c >= 1; --c)
+      if (fits(c, c, a)) { s = c; break; }
+    if (s > ks && (a == 0 || ks < 2)) { ks = vs = s; alias = a; }
+  }
+  if (ks == 0) {
+    for (int a = 0; a <= 1 && ks == 0; ++a)
+      if (fits(2, 1, a)) { ks = 2; vs = 1; alias = a; }
+  }
+  if (ks == 0) return fail(NSA_ERR_UNSUPPORTED, "tile does not fit in shared memory");
+  if (ks < nsa::kMaxStages && fits(ks + 1, vs, alias)) ++ks;
+  const char* env_ks = getenv("NSA_SEL_KSTAGES");
+  const char* env_vs = getenv("NSA_SEL_VSTAGES");
+  if (env_ks != nullptr || env_vs != nullptr) {
+    const int eks = env_ks ? atoi(env_ks) : ks, evs = env_vs ? atoi(env_vs) : vs;
+    if (eks >= 1 && evs >= 1 && eks <= nsa::kMaxStages && evs <= nsa::kMaxStages) {
+      if (fits(eks, evs, alias)) {
+        ks = eks;
+        vs = evs;
+      } else if (fits(eks, evs, 1)) {
+        ks = eks;
+        vs = evs;
+        alias = 1;
+      }
+    }
+  }
+  pl->KS = ks;
+  pl->VS = vs;
+  pl->alias = alias;
+  pl->layout = V.layout(ks, vs, pl->maxsub, alias);
+  int grid = sm_count > 0 ? sm_count : 148;
+  if (d->max_ctas > 0 && d->max_ctas < grid) grid = d->max_ctas;
+  if (grid > pl->n_units) grid = pl->n_units;
+  pl->grid = grid;
+  return NSA_OK;
+}
+
+int encode(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* ptr, const cuuint64_t* dims,
+           const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle sw, CUtensorMapL2promotion prom,
+           const char* what) {
+  PFN_cuTensorMapEncodeTiled_v12000 f = encode_fn();
+  if (f == nullptr) return fail(NSA_ERR_DRIVER, "cuTensorMapEncodeTiled is unavailable from the driver");
+  cuuint32_t es[5] = {1, 1, 1, 1, 1};
+  CUresult r = f(m, dt, (cuuint32_t)rank, const_cast<void*>(ptr), dims, strides, box, es,
+                 CU_TENSOR_MAP_INTERLEAVE_NONE, sw, prom, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(NSA_ERR_INVALID_ARG, "cuTensorMapEncodeTiled(%s) failed with %d", what, (int)r);
+  return NSA_OK;
+}
+
+int launch(const nsa_sel_desc* d, nsa_stream_t stream) {
+  int sm = 0, dev = 0;
+  int rc = current_sm_count(&sm, &dev);
+  if (rc != NSA_OK) return rc;
+  Plan pl;
+  rc = make_plan(d, sm, &pl);
+  if (rc != NSA_OK) return rc;
+  int nv = 0;
+  const Variant& V = variants(&nv)[pl.variant];
+
+  const int B = d->batch, Hq = d->heads_q, Hkv = d->heads_kv, T = d->seq_len;
+  const cuuint64_t dqk = (cuuint64_t)d->d_qk, dv = (cuuint64_t)d->d_v;
+  CUtensorMap tmQ, tmK, tmV, tmO;
+  {
+    cuuint64_t dims[4] = {dqk, (cuuint64_t)T, (cuuint64_t)Hq, (cuuint64_t)B};
+    cuuint64_t str[3] = {dqk * 2, dqk * 2 * T, dqk * 2 * T * Hq};
+    cuuint32_t box[4] = {64, (cuuint32_t)pl.BQs, (cuuint32_t)pl.G, 1};
+    rc = encode(&tmQ, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, d->q, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_128B, "Q");
+    if (rc != NSA_OK) return rc;
+  }
+  {
+    cuuint64_t dims[3] = {dqk, (cuuint64_t)T, (cuuint64_t)B * Hkv};
+    cuuint64_t str[2] = {dqk * 2, dqk * 2 * T};
+    cuuint32_t box[3] = {64, 64, 1};
+    rc = encode(&tmK, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, d->k, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "K");
+    if (rc != NSA_OK) return rc;
+  }
+  {
+    cuuint64_t dims[3] = {dv, (cuuint64_t)T, (cuuint64_t)B * Hkv};
+    cuuint64_t str[2] = {dv * 2, dv * 2 * T};
+    cuuint32_t box[3] = {64, 64, 1};
+    rc = encode(&tmV, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, d->v, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "V");
+    if (rc != NSA_OK) return rc;
+  }
+  {
+    const bool f32 = d->o_dtype == NSA_DTYPE_F32;
+    const cuuint64_t es = f32 ? 4 : 2;
+    cuuint64_t dims[4] = {dv, (cuuint64_t)T, (cuuint64_t)Hq, (cuuint64_t)B};
+    cuuint64_t str[3] = {dv * es, dv * es * T, dv * es * T * Hq};
+    cuuint32_t box[4] = {64, (cuuint32_t)pl.BQs, (cuuint32_t)pl.G, 1};
+    rc = encode(&tmO, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, d->o, dims, str,
+                box, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, "O");
+    if (rc != NSA_OK) return rc;
+  }
+
+  nsa::Params p{};
+  p.sel = d->sel;
+  p.cu_seqlens = d->cu_seqlens;
+  p.lse = d->lse;
+  p.cyc = d->cyc;
+  p.err = d->err;
+  p.B = B;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.T = T;
+  p.G = pl.G;
+  p.LP = d->block_size;
+  p.BQ = d->q_block;
+  p.BQs = pl.BQs;
+  p.parts = pl.parts;
+  p.NQB = d->n_qblocks;
+  p.KSEL = d->n_sel;
+  p.n_seq = d->cu_seqlens ? d->n_seqs : 1;
+  p.bkv_begin = pl.bkv_begin;
+  p.bkv_end = pl.bkv_end;
+  p.qb_begin = pl.qb_begin;
+  p.qb_end = pl.qb_end;
+  p.n_units = pl.n_units;
+  p.maxsub = pl.maxsub;
+  p.KS = pl.KS;
+  p.VS = pl.VS;
+  const double scale = d->scale > 0.f ? (double)d->scale : 1.0 / sqrt((double)d->d_qk);
+  p.scale_log2 = (float)(scale * 1.4426950408889634074);
+  int tmo = d->timeout_ms;
+  if (tmo <= 0) {
+    const char* e = getenv("NSA_SEL_TIMEOUT_MS");
+    tmo = e ? atoi(e) : 0;
+    if (tmo <= 0) tmo = 2000;
+  }
+  p.timeout_ns = (unsigned long long)tmo * 1000000ull;
+  p.off_k = pl.layout.off_k;
+  p.off_v = pl.layout.off_v;
+  p.off_q = pl.layout.off_q;
+  p.off_p = pl.layout.off_p;
+  p.off_out = pl.layout.off_out;
+  p.off_tr = pl.layout.off_tr;
+  p.off_alpha = pl.layout.off_alpha;
+  p.off_inv = pl.layout.off_inv;
+  p.off_info = pl.layout.off_info;
+  p.off_bar = pl.layout.off_bar;
+  p.stage_alias = pl.alias;
+  p.debug_stall = (d->debug_flags & NSA_DEBUG_STALL) ? 1 : 0;
+
+  {
+    std::lock_guard<std::mutex> lk(g_dev.mu);
+    const uint64_t bit = 1ull << pl.variant;
+    if ((g_dev.attr_done[dev] & bit) == 0) {
+      cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(V.kernel),
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
+      g_dev.attr_done[dev] |= bit;
+    }
+  }
+  void* args[] = {&tmQ, &tmK, &tmV, &tmO, &p};
+  cudaError_t e = cudaLaunchKernel(reinterpret_cast<const void*>(V.kernel), dim3(pl.grid), dim3(nsa::kThreads), args,
+                                   pl.layout.total, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
+  g_last_error[0] = '\0';
+  return NSA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int nsa_sel_run(const nsa_sel_desc* desc, nsa_stream_t stream) { return launch(desc, stream); }
+
+int nsa_sel_plan(const nsa_sel_desc* desc, int32_t sm_count, nsa_sel_plan_info* out) {
+  if (out == nullptr) return fail(NSA_ERR_INVALID_ARG, "out is NULL");
+  int sm = sm_count;
+  if (sm <= 0) {
+    int dev = 0;
+    int rc = current_sm_count(&sm, &dev);
+    if (rc != NSA_OK) return rc;
+  }
+  Plan pl;
+  int rc = make_plan(desc, sm, &pl);
+  if (rc != NSA_OK) return rc;
+  int nv = 0;
+  const Variant& V = variants(&nv)[pl.variant];
+  memset(out, 0, sizeof(*out));
+  out->n_cols = pl.ncol;
+  out->q_per_unit = pl.BQs;
+  out->parts = pl.parts;
+  out->n_units = pl.n_units;
+  out->k_stages = pl.KS;
+  out->v_stages = pl.VS;
+  out->smem_bytes = (int32_t)pl.layout.total;
+  out->grid = pl.grid;
+  out->tmem_cols = V.tmem_cols;
+  g_last_error[0] = '\0';
+  return NSA_OK;
+}
+
+int nsa_sel_forward(const void* q, const void* k, const void* v, const int32_t* sel, float* o, int64_t* cyc,
+                    int32_t B, int32_t Hq, int32_t Hkv, int32_t S, int32_t D, int32_t NQB, int32_t KSEL,
+                    int32_t l_prime, int32_t BQ, nsa_stream_t stream) {
+  nsa_sel_desc d;
+  memset(&d, 0, sizeof(d));
+  d.q = q;
+  d.k = k;
+  d.v = v;
+  d.sel = sel;
+  d.o = o;
+  d.cyc = cyc;
+  d.batch = B;
+  d.heads_q = Hq;
+  d.heads_kv = Hkv;
+  d.seq_len = S;
+  d.d_qk = D;
+  d.d_v = D;
+  d.n_qblocks = NQB;
+  d.n_sel = KSEL;
+  d.block_size = l_prime;
+  d.q_block = BQ;
+  d.o_dtype = NSA_DTYPE_F32;
+  return launch(&d, stream);
+}
+
+int nsa_sel_forward_lse(const void* q, const void* k, const void* v, const int32_t* sel,
+                        const int32_t* cu_seqlens, int32_t n_seqs, void* o, float* lse, int32_t o_dtype, int32_t B,
+                        int32_t Hq, int32_t Hkv, int32_t T, int32_t d_qk, int32_t d_v, int32_t NQB, int32_t KSEL,
+                        int32_t l_prime, int32_t BQ, float scale, nsa_stream_t stream) {
+  nsa_sel_desc d;
+  memset(&d, 0, sizeof(d));
+  d.q = q;
+  d.k = k;
+  d.v = v;
+  d.sel = sel;
+  d.cu_seqlens = cu_seqlens;
+  d.n_seqs = n_seqs;
+  d.o = o;
+  d.lse = lse;
+  d.batch = B;
+  d.heads_q = Hq;
+  d.heads_kv = Hkv;
+  d.seq_len = T;
+  d.d_qk = d_qk;
+  d.d_v = d_v;
+  d.n_qblocks = NQB;
+  d.n_sel = KSEL;
+  d.block_size = l_prime;
+  d.q_block = BQ;
+  d.o_dtype = o_dtype;
+  d.scale = scale;
+  return launch(&d, stream);
+}
+
+const char* nsa_sel_last_error(void) { return g_last_error; }
+
+int32_t nsa_sel_version(void) { return NSA_SEL_VERSION; }
+
+}  // extern "C"

@@ -1,0 +1,165 @@
+// PyTorch extension with the reference's op signature, over the C ABI of libnsa_sel.so.
+//
+//   forward(Q, K, V, sel, l_prime, BQ, cyc) -> O (fp32)
+//       same arguments, meaning and errors as the reference's pybind op
+//       (nsa_v2.cu:147-170, nsa_v1.cu:125-147, nsa_v0.cu:118-146): Q [B,Hq,S,D] bf16,
+//       K/V [B,Hkv,S,D] bf16, sel int32 [B,Hkv,NQB,KSEL], cyc int64 [NQB*B*Hkv*2] or empty.
+//       Unsupported shapes raise RuntimeError (TORCH_CHECK), as in the reference.
+//   forward_lse(Q, K, V, sel, l_prime, BQ, cu_seqlens=None, scale=0, out_f32=False)
+//       -> (O bf16 (or fp32), LSE fp32 [B,Hq,T]); d_qk may differ from d_v; optional varlen.
+//
+// The translation unit holds no device code, so it also builds when a harness compiles it
+// with the reference's flags (e.g. `-arch=sm_90a`).  libnsa_sel.so is opened at first use
+// from the directory of this extension, or from the package directory next to this source.
+#include <dlfcn.h>
+#include <torch/extension.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+
+#include <mutex>
+#include <string>
+
+#include "../../include/nsa_sel.h"
+
+namespace {
+
+struct Api {
+  decltype(&nsa_sel_forward) forward = nullptr;
+  decltype(&nsa_sel_run) run = nullptr;
+  decltype(&nsa_sel_last_error) last_error = nullptr;
+  decltype(&nsa_sel_version) version = nullptr;
+};
+
+std::string dir_of(const std::string& path) {
+  const size_t p = path.find_last_of('/');
+  return p == std::string::npos ? std::string(".") : path.substr(0, p);
+}
+
+const Api& api() {
+  static Api a;
+  static std::once_flag once;
+  static std::string error;
+  std::call_once(once, [] {
+    std::string candidates[3];
+    Dl_info info;
+    if (dladdr(reinterpret_cast<void*>(&dir_of), &info) != 0 && info.dli_fname != nullptr)
+      candidates[0] = dir_of(info.dli_fname) + "/libnsa_sel.so";
+    candidates[1] = dir_of(dir_of(__FILE__)) + "/libnsa_sel.so";  // <pkg>/csrc/.. = <pkg>
+    if (const char* env = getenv("NSA_SEL_LIBRARY")) candidates[2] = env;
+    void* h = nullptr;
+    for (const std::string& c : candidates) {
+      if (c.empty()) continue;
+      h = dlopen(c.c_str(), RTLD_NOW | RTLD_LOCAL);
+      if (h != nullptr) break;
+      error += c + ": " + dlerror() + "; ";
+    }
+    if (h == nullptr) return;
+    a.forward = reinterpret_cast<decltype(a.forward)>(dlsym(h, "nsa_sel_forward"));
+    a.run = reinterpret_cast<decltype(a.run)>(dlsym(h, "nsa_sel_run"));
+    a.last_error = reinterpret_cast<decltype(a.last_error)>(dlsym(h, "nsa_sel_last_error"));
+    a.version = reinterpret_cast<decltype(a.version)>(dlsym(h, "nsa_sel_version"));
+  });
+  TORCH_CHECK(a.forward && a.run && a.last_error && a.version,
+              "libnsa_sel.so could not be loaded (build it first): ", error);
+  return a;
+}
+
+void check_inputs(const torch::Tensor& Q, const torch::Tensor& K, const torch::Tensor& V, const torch::Tensor& sel) {
+  TORCH_CHECK(Q.is_cuda() && K.is_cuda() && V.is_cuda() && sel.is_cuda(), "Q, K, V and sel must be CUDA tensors");
+  TORCH_CHECK(Q.scalar_type() == at::kBFloat16 && K.scalar_type() == at::kBFloat16 &&
+                  V.scalar_type() == at::kBFloat16,
+              "Q, K and V must be bfloat16");
+  TORCH_CHECK(sel.scalar_type() == at::kInt, "sel must be int32");
+  TORCH_CHECK(Q.dim() == 4 && K.dim() == 4 && V.dim() == 4 && sel.dim() == 4,
+              "expected Q/K/V [B,H,S,D] and sel [B,Hkv,NQB,KSEL]");
+  TORCH_CHECK(Q.is_contiguous() && K.is_contiguous() && V.is_contiguous() && sel.is_contiguous(),
+              "Q, K, V and sel must be contiguous");
+  TORCH_CHECK(K.size(0) == Q.size(0) && V.size(0) == Q.size(0) && sel.size(0) == Q.size(0), "batch mismatch");
+  TORCH_CHECK(K.size(2) == Q.size(2) && V.size(2) == Q.size(2), "sequence length mismatch");
+  TORCH_CHECK(V.size(1) == K.size(1) && sel.size(1) == K.size(1), "KV head count mismatch");
+  TORCH_CHECK(K.size(3) == Q.size(3), "Q and K head dims differ");
+  TORCH_CHECK(K.get_device() == Q.get_device() && V.get_device() == Q.get_device() &&
+                  sel.get_device() == Q.get_device(),
+              "all tensors must be on one device");
+}
+
+int32_t i32(int64_t x, const char* what) {
+  TORCH_CHECK(x >= 0 && x < (int64_t(1) << 31), what, " out of int32 range");
+  return static_cast<int32_t>(x);
+}
+
+torch::Tensor forward(torch::Tensor Q, torch::Tensor K, torch::Tensor V, torch::Tensor sel, int64_t l_prime,
+                      int64_t BQ, torch::Tensor cyc) {
+  check_inputs(Q, K, V, sel);
+  TORCH_CHECK(V.size(3) == Q.size(3), "forward() needs d_v == d_qk (use forward_lse for d_qk != d_v)");
+  const Api& a = api();
+  const c10::cuda::CUDAGuard guard(Q.device());
+  auto O = torch::empty({Q.size(0), Q.size(1), Q.size(2), V.size(3)}, Q.options().dtype(torch::kFloat32));
+  int64_t* cyc_ptr = nullptr;
+  if (cyc.defined() && cyc.numel() > 0) {
+    TORCH_CHECK(cyc.is_cuda() && cyc.scalar_type() == at::kLong && cyc.is_contiguous(), "cyc must be CUDA int64");
+    TORCH_CHECK(cyc.numel() >= sel.size(2) * sel.size(0) * sel.size(1) * 2, "cyc must hold NQB*B*Hkv*2 entries");
+    cyc_ptr = cyc.data_ptr<int64_t>();
+  }
+  const int rc = a.forward(Q.data_ptr(), K.data_ptr(), V.data_ptr(), sel.data_ptr<int32_t>(), O.data_ptr<float>(),
+                           cyc_ptr, i32(Q.size(0), "B"), i32(Q.size(1), "Hq"), i32(K.size(1), "Hkv"),
+                           i32(Q.size(2), "S"), i32(Q.size(3), "D"), i32(sel.size(2), "NQB"),
+                           i32(sel.size(3), "KSEL"), i32(l_prime, "l_prime"), i32(BQ, "BQ"),
+                           reinterpret_cast<nsa_stream_t>(c10::cuda::getCurrentCUDAStream().stream()));
+  TORCH_CHECK(rc == NSA_OK, "nsa_sel_forward failed (", rc, "): ", a.last_error());
+  return O;
+}
+
+std::vector<torch::Tensor> forward_lse(torch::Tensor Q, torch::Tensor K, torch::Tensor V, torch::Tensor sel,
+                                       int64_t l_prime, int64_t BQ, c10::optional<torch::Tensor> cu_seqlens,
+                                       double scale, bool out_f32) {
+  check_inputs(Q, K, V, sel);
+  const Api& a = api();
+  const c10::cuda::CUDAGuard guard(Q.device());
+  auto O = torch::empty({Q.size(0), Q.size(1), Q.size(2), V.size(3)},
+                        Q.options().dtype(out_f32 ? torch::kFloat32 : torch::kBFloat16));
+  auto L = torch::empty({Q.size(0), Q.size(1), Q.size(2)}, Q.options().dtype(torch::kFloat32));
+  nsa_sel_desc d;
+  memset(&d, 0, sizeof(d));
+  d.q = Q.data_ptr();
+  d.k = K.data_ptr();
+  d.v = V.data_ptr();
+  d.sel = sel.data_ptr<int32_t>();
+  if (cu_seqlens.has_value() && cu_seqlens->defined()) {
+    const auto& cu = *cu_seqlens;
+    TORCH_CHECK(cu.is_cuda() && cu.scalar_type() == at::kInt && cu.dim() == 1 && cu.is_contiguous(),
+                "cu_seqlens must be a contiguous CUDA int32 vector");
+    d.cu_seqlens = cu.data_ptr<int32_t>();
+    d.n_seqs = i32(cu.numel() - 1, "n_seqs");
+  }
+  d.o = O.data_ptr();
+  d.lse = L.data_ptr<float>();
+  d.batch = i32(Q.size(0), "B");
+  d.heads_q = i32(Q.size(1), "Hq");
+  d.heads_kv = i32(K.size(1), "Hkv");
+  d.seq_len = i32(Q.size(2), "T");
+  d.d_qk = i32(Q.size(3), "d_qk");
+  d.d_v = i32(V.size(3), "d_v");
+  d.n_qblocks = i32(sel.size(2), "NQB");
+  d.n_sel = i32(sel.size(3), "KSEL");
+  d.block_size = i32(l_prime, "l_prime");
+  d.q_block = i32(BQ, "BQ");
+  d.o_dtype = out_f32 ? NSA_DTYPE_F32 : NSA_DTYPE_BF16;
+  d.scale = static_cast<float>(scale);
+  const int rc = a.run(&d, reinterpret_cast<nsa_stream_t>(c10::cuda::getCurrentCUDAStream().stream()));
+  TORCH_CHECK(rc == NSA_OK, "nsa_sel_run failed (", rc, "): ", a.last_error());
+  return {O, L};
+}
+
+int64_t library_version() { return api().version(); }
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "B200 NSA selected-branch forward (sm_100a) with the nsa-hopper op signature";
+  m.def("forward", &forward, "forward(Q, K, V, sel, l_prime, BQ, cyc) -> O (fp32)");
+  m.def("forward_lse", &forward_lse, "forward_lse(Q, K, V, sel, l_prime, BQ, cu_seqlens, scale, out_f32) -> [O, LSE]",
+        py::arg("Q"), py::arg("K"), py::arg("V"), py::arg("sel"), py::arg("l_prime"), py::arg("BQ"),
+        py::arg("cu_seqlens") = py::none(), py::arg("scale") = 0.0, py::arg("out_f32") = false);
+  m.def("library_version", &library_version);
+}

@@ -1,0 +1,38 @@
+"""PyTorch-facing ops: the reference's ``forward`` signature plus the BASELINE ``forward_lse``.
+
+These call the in-tree extension ``nsa_hopper_b200._C`` (nsa_sel_torch.cpp), which calls the C
+ABI of ``libnsa_sel.so``.  There is no CPU or eager fallback: if the extension or the library
+is missing, or the device is not a B200, the call raises.
+"""
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+
+try:
+    from . import _C  # type: ignore[attr-defined]
+except ImportError as e:  # pragma: no cover - exercised only when the build is missing
+    raise ImportError("nsa_hopper_b200._C is not built: run `python -m nsa_hopper_b200.build`") from e
+
+
+def forward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, sel: torch.Tensor, l_prime: int, BQ: int,
+            cyc: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Drop-in for the reference op ``mod.forward(Q,K,V,sel,l_prime,BQ,cyc)`` (nsa_v2.cu:147):
+    returns fp32 O [B,Hq,S,D].  ``cyc`` may be an int64 CUDA tensor of NQB*B*Hkv*2 entries
+    (accumulated into) or empty/None."""
+    if cyc is None:
+        cyc = torch.empty(0, dtype=torch.int64, device=Q.device)
+    return _C.forward(Q, K, V, sel, int(l_prime), int(BQ), cyc)
+
+
+def forward_lse(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, sel: torch.Tensor, l_prime: int = 64,
+                BQ: int = 1, cu_seqlens: Optional[torch.Tensor] = None, scale: float = 0.0,
+                out_f32: bool = False) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Selected-branch forward returning (O bf16 [B,Hq,T,d_v], LSE fp32 [B,Hq,T])."""
+    o, lse = _C.forward_lse(Q, K, V, sel, int(l_prime), int(BQ), cu_seqlens, float(scale), bool(out_f32))
+    return o, lse
+
+
+def library_version() -> int:
+    return int(_C.library_version())
