@@ -1,0 +1,407 @@
+"""Benchmark of the NSA selected-branch forward on B200 (one JSON line on rank 0).
+
+Default: the north-star workload (B=1 per GPU, T=65536, Hq=64, Hkv=4, D=128, block 64,
+top-n=16, BASELINE rule 0 indices) on one GPU.  A "step" is one forward over the whole
+workload.  Under torchrun each rank runs its own independent shard (weak scaling: rank r owns
+sequence r of a batch of N sequences; no collective on the data path).  ``--scaling strong``
+instead splits one workload over the ranks by (KV head, query-token range).
+
+Timing: W untimed warm-up steps, then K steps, each timed with CUDA events on the launching
+stream; between timed steps a 256 MiB buffer is written to flush L2 (outside the events).  The
+timed loop is bracketed by a barrier and torch.cuda.synchronize(); the per-step time reported is
+the max over ranks of each rank's mean.  ``e2e`` repeats the measurement through the C ABI with
+pinned host inputs copied in and O/LSE copied out inside the timed region.
+
+``--impl reference`` times the CPU implementation of the same path (the oracle restatement of
+the reference's PyTorch code, fp32, all host threads) on a bounded sample of the workload.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "selected-attn fwd TFLOP/s & tokens/s at T=64K, 1/2/4/8 B200; % of roofline"
+FLUSH_BYTES = 256 << 20
+
+
+def _env_int(name, default):
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+def measured_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            j = json.load(f)
+        return float(j["hbm_gbs"]), float(j["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def committed_traffic(workload: str):
+    """DRAM bytes per launch from a committed ncu summary (profiles/), or None."""
+    path = os.path.join(REPO, "profiles", f"nsa_sel_fwd_{workload}.traffic.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["dram_bytes_per_launch"])
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.out = ""
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                self.out = ""
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in (self.out or "").splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, val in zip(names, f[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def reduce_max(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    import torch
+
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def shard_for(args, w, rank, world):
+    """(seed, shard tuple or None) of this rank."""
+    from nsa_hopper_b200 import shard
+
+    if args.scaling == "weak" or world == 1:
+        return args.seed + rank, None
+    plans = shard.plan_strong(w.B, w.Hkv, w.T, world)
+    return args.seed, plans[rank]
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+
+    from nsa_hopper_b200 import capi, workload
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    w = workload.CONFIGS[args.config]
+    if w.n_seqs:
+        raise SystemExit("bench.py times the fixed-shape configs; cfg4 (varlen) is covered by tests")
+    seed, sh = shard_for(args, w, rank, world)
+    B, T, Hq, Hkv = w.B, w.T, w.Hq, w.Hkv
+
+    # Inputs: Q/K/V N(0,1) from a seeded device generator rounded to bf16; indices from the
+    # seeded host generator (identical on every host).
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    q = torch.randn(B, Hq, T, w.d_qk, device=dev, generator=gen).to(torch.bfloat16)
+    k = torch.randn(B, Hkv, T, w.d_qk, device=dev, generator=gen).to(torch.bfloat16)
+    v = torch.randn(B, Hkv, T, w.d_v, device=dev, generator=gen).to(torch.bfloat16)
+    sel_np = workload.make_indices(w, seed=seed)
+    sel = torch.from_numpy(sel_np).to(dev)
+    o = torch.empty(B, Hq, T, w.d_v, device=dev, dtype=torch.bfloat16)
+    lse = torch.empty(B, Hq, T, device=dev, dtype=torch.float32)
+    err = torch.zeros(1, device=dev, dtype=torch.int32)
+    flush = torch.empty(FLUSH_BYTES // 4, device=dev, dtype=torch.float32)
+
+    work = workload.algorithmic_work(w, sel_np)
+    frac_units = 1.0
+    if sh is not None:  # strong scaling: this rank's fraction of the rows
+        bkv0, bkv1, qb0, qb1 = sh
+        frac_units = (bkv1 - bkv0) * (qb1 - qb0) / float(B * Hkv * T)
+
+    def desc(qp, kp, vp, sp, op, lp):
+        d = capi.make_desc(q=qp, k=kp, v=vp, sel=sp, o=op, lse=lp, err=err.data_ptr(), batch=B, heads_q=Hq,
+                           heads_kv=Hkv, seq_len=T, d_qk=w.d_qk, d_v=w.d_v, n_qblocks=T, n_sel=w.n,
+                           block_size=w.block, q_block=1, o_dtype=capi.DTYPE_BF16)
+        if sh is not None:
+            d.bkv_begin, d.bkv_end, d.qb_begin, d.qb_end = sh
+        return d
+
+    d_dev = desc(q.data_ptr(), k.data_ptr(), v.data_ptr(), sel.data_ptr(), o.data_ptr(), lse.data_ptr())
+    stream = torch.cuda.current_stream(dev)
+    sh_ = stream.cuda_stream
+
+    for _ in range(args.warmup):
+        capi.run(d_dev, sh_)
+    torch.cuda.synchronize()
+    if int(err.item()) != 0:
+        raise RuntimeError(f"kernel reported device error {int(err.item())}")
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier(world)
+    with ClockSampler(local_rank) as clk:
+        for i in range(args.steps):
+            flush.fill_(float(i))
+            starts[i].record(stream)
+            capi.run(d_dev, sh_)
+            ends[i].record(stream)
+        barrier(world)
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    mean_ms = statistics.mean(step_ms)
+    max_ms = reduce_max(mean_ms, world)
+    if int(err.item()) != 0:
+        raise RuntimeError(f"kernel reported device error {int(err.item())}")
+
+    # ---- end to end through the C ABI with host buffers
+    e2e = None
+    if not args.no_e2e:
+        hq = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
+        hk = torch.empty(k.shape, dtype=k.dtype, pin_memory=True)
+        hv = torch.empty(v.shape, dtype=v.dtype, pin_memory=True)
+        hs = torch.empty(sel.shape, dtype=sel.dtype, pin_memory=True)
+        ho = torch.empty(o.shape, dtype=o.dtype, pin_memory=True)
+        hl = torch.empty(lse.shape, dtype=lse.dtype, pin_memory=True)
+        hq.copy_(q)
+        hk.copy_(k)
+        hv.copy_(v)
+        hs.copy_(sel)
+        dq, dk, dv_, ds = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v), torch.empty_like(sel)
+        d_e2e = desc(dq.data_ptr(), dk.data_ptr(), dv_.data_ptr(), ds.data_ptr(), o.data_ptr(), lse.data_ptr())
+        h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hs))
+        d2h = ho.numel() * ho.element_size() + hl.numel() * hl.element_size()
+        ksteps = max(1, min(args.steps, 5))
+
+        def e2e_step():
+            dq.copy_(hq, non_blocking=True)
+            dk.copy_(hk, non_blocking=True)
+            dv_.copy_(hv, non_blocking=True)
+            ds.copy_(hs, non_blocking=True)
+            capi.run(d_e2e, sh_)
+            ho.copy_(o, non_blocking=True)
+            hl.copy_(lse, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        barrier(world)
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for _ in range(ksteps):
+            e2e_step()
+        ev1.record(stream)
+        barrier(world)
+        e2e_ms = reduce_max(ev0.elapsed_time(ev1) / ksteps, world)
+        tok = work["tokens"] * frac_units * world
+        e2e = {"value": tok / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": ksteps,
+               "path": "C ABI nsa_sel_run with pinned host Q/K/V/sel in, O/LSE out"}
+
+    hbm_peak, tf_peak, peak_kind = measured_peaks()
+    tokens_job = work["tokens"] * frac_units * world
+    flops_rank = work["flops"] * frac_units
+    bytes_rank = work["bytes"] * frac_units
+    achieved_gbs = bytes_rank / (mean_ms * 1e-3) / 1e9
+    traffic = committed_traffic(args.config) if (sh is None and args.config == "ns") else None
+    clocks = clk.summary()
+    result = None
+    if rank == 0:
+        result = {
+            "metric": METRIC,
+            "value": tokens_job / (max_ms * 1e-3),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": max_ms,
+            "higher_is_better": True,
+            "scaling": args.scaling if world > 1 else "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic: N(0,1) Q/K/V rounded to bf16, seeded BASELINE index rule",
+            "config": {"workload": args.config, "B_per_rank": w.B if sh is None else w.B, "T": T, "Hq": Hq,
+                       "Hkv": Hkv, "d_qk": w.d_qk, "d_v": w.d_v, "block": w.block, "top_n": w.n, "rule": w.rule,
+                       "parallelism": f"{args.scaling} shards over {world} GPU(s), no collective",
+                       "l2": "256 MiB buffer written between timed steps (L2 flushed)"},
+            "tflops": flops_rank * world / (max_ms * 1e-3) / 1e12 if sh is None else
+            work["flops"] / (max_ms * 1e-3) / 1e12,
+            "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": achieved_gbs / hbm_peak, "traffic": traffic,
+                         "peak_kind": peak_kind,
+                         "algorithmic_bytes_per_launch": bytes_rank,
+                         "tensor_frac": flops_rank / (mean_ms * 1e-3) / (tf_peak * 1e12),
+                         "kernel_ms": mean_ms},
+            "e2e": e2e,
+            "clocks": clocks,
+            "gpu_launches": args.steps,
+            "step_ms": step_ms,
+        }
+    return result
+
+
+def cpu_baseline(args, seconds: float = 12.0):
+    """Oracle (fp32, all host threads) on a bounded sample of the same workload: the last
+    tokens of the sequence (full top-n cost), all KV heads.  Returns a dict."""
+    import torch
+
+    import oracle
+    from nsa_hopper_b200 import workload
+
+    w = workload.CONFIGS[args.config]
+    g = torch.Generator().manual_seed(args.seed)
+    T = w.T
+    # Only the rows the sample touches need real Q; K/V must be whole for the gather.
+    k = torch.randn(w.B, w.Hkv, T, w.d_qk, generator=g).to(torch.bfloat16)
+    v = torch.randn(w.B, w.Hkv, T, w.d_v, generator=g).to(torch.bfloat16)
+    q = torch.zeros(w.B, w.Hq, T, w.d_qk, dtype=torch.bfloat16)
+    sel = workload.make_indices(w, seed=args.seed)
+    threads = oracle.default_threads()
+    ntok = 16
+    t0 = time.time()
+    while True:
+        tb = T - ntok
+        q[:, :, tb:T] = torch.randn(w.B, w.Hq, ntok, w.d_qk, generator=g).to(torch.bfloat16)
+        t1 = time.time()
+        oracle.forward(q, k, v, sel, w.block, 1, f32=True, t_range=(tb, T), threads=threads)
+        dt = time.time() - t1
+        if dt > seconds / 4 or ntok >= T or time.time() - t0 > seconds:
+            break
+        ntok = min(T, ntok * 4)
+    return {"value": w.B * ntok / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"last {ntok} tokens x {w.B * w.Hkv} (batch, KV head) rows of '{args.config}', fp32, "
+                      f"{dt:.2f} s", "seconds": dt}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    from nsa_hopper_b200 import workload
+
+    w = workload.CONFIGS[args.config]
+    res = None
+    times = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_baseline(args, seconds=8.0 if i >= args.warmup else 2.0)
+        if i >= args.warmup:
+            times.append(r)
+        res = r
+    val = statistics.mean(x["value"] for x in times)
+    return {
+        "metric": METRIC, "value": val, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": w.T / val * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+        "config": {"workload": args.config, "T": w.T, "Hq": w.Hq, "Hkv": w.Hkv, "d_qk": w.d_qk, "d_v": w.d_v,
+                   "block": w.block, "top_n": w.n, "rule": w.rule},
+        "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", default="ns")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = _env_int("WORLD_SIZE", 1)
+    rank = _env_int("RANK", 0)
+    local_rank = _env_int("LOCAL_RANK", 0)
+
+    if args.impl == "reference":
+        res = run_reference(args, rank, world)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        res = run_ours(args, rank, world, local_rank)
+        if rank == 0:
+            if world == 1 and not args.no_cpu_baseline:
+                cb = cpu_baseline(args)
+                res["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+            else:
+                res["cpu_baseline"] = None
+            print(json.dumps(res), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

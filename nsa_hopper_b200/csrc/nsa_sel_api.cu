@@ -95,19 +95,21 @@ typedef void (*KernelFn)(const CUtensorMap, const CUtensorMap, const CUtensorMap
 typedef nsa::SmemLayout (*LayoutFn)(int, int, int, int);
 
 struct Variant {
-  int dqk, dv, ncol, out_f32;
+  int dqk, dv, ncol, out_f32, nwg, threads;
   KernelFn kernel;
   LayoutFn layout;
   int k_stage, v_stage, tmem_cols;
 };
 
-template <int DQK, int DV, int NCOL, typename OutT>
+template <int DQK, int DV, int NCOL, typename OutT, int NWG>
 Variant make_variant() {
-  using C = nsa::Cfg<DQK, DV, NCOL, OutT>;
+  using C = nsa::Cfg<DQK, DV, NCOL, OutT, NWG>;
   return Variant{DQK,
                  DV,
                  NCOL,
                  sizeof(OutT) == 4 ? 1 : 0,
+                 NWG,
+                 C::kThreads,
                  reinterpret_cast<KernelFn>(&nsa::nsa_sel_fwd_kernel<C>),
                  &nsa::smem_layout<C>,
                  C::kKStage,
@@ -115,9 +117,12 @@ Variant make_variant() {
                  C::kTmemCols};
 }
 
-#define NSA_VARIANTS_FOR(DQK, DV)                                                                         \
-  make_variant<DQK, DV, 16, bf16>(), make_variant<DQK, DV, 32, bf16>(), make_variant<DQK, DV, 64, bf16>(), \
-      make_variant<DQK, DV, 16, float>(), make_variant<DQK, DV, 32, float>(), make_variant<DQK, DV, 64, float>()
+// Narrow tiles (N = 16: per-token selection with G <= 16) split every unit's chunks over two
+// softmax warpgroups; wider tiles (per-query-block selection) use one.
+#define NSA_VARIANTS_FOR(DQK, DV)                                                                      \
+  make_variant<DQK, DV, 16, bf16, 2>(), make_variant<DQK, DV, 32, bf16, 1>(),                           \
+      make_variant<DQK, DV, 64, bf16, 1>(), make_variant<DQK, DV, 16, float, 2>(),                      \
+      make_variant<DQK, DV, 32, float, 1>(), make_variant<DQK, DV, 64, float, 1>()
 
 const Variant* variants(int* n) {
   static const Variant v[] = {NSA_VARIANTS_FOR(64, 64), NSA_VARIANTS_FOR(128, 128), NSA_VARIANTS_FOR(192, 128)};
@@ -135,7 +140,7 @@ int find_variant(int dqk, int dv, int ncol, int out_f32) {
 
 // ------------------------------------------------------------------ planning
 struct Plan {
-  int G, BQs, parts, ncol, maxsub, n_units, KS, VS, alias, grid, variant;
+  int G, BQs, parts, ncol, maxsub, n_units, KS, VS, out_bufs, grid, variant;
   int bkv_begin, bkv_end, qb_begin, qb_end;
   nsa::SmemLayout layout;
 };
@@ -212,42 +217,34 @@ int make_plan(const nsa_sel_desc* d, int sm_count, Plan* pl) {
   if (units >= (1ll << 31)) return fail(NSA_ERR_UNSUPPORTED, "too many work units");
   pl->n_units = (int)units;
 
-  // Ring depths: the deepest equal K/V rings that fit, then one more K stage if it fits.  The
-  // output staging tile gets its own double buffer unless aliasing it into the transpose
-  // buffer buys a deeper ring (wide tiles).
-  auto fits = [&](int k, int v, int a) { return (int)V.layout(k, v, pl->maxsub, a).total <= kSmemLimit; };
-  int ks = 0, vs = 0, alias = 0;
-  for (int a = 0; a <= 1; ++a) {
-    int s = 0;
+  // Ring depths: the deepest equal K/V rings that fit, then one more K stage if it fits (the
+  // score MMAs run ahead of the softmax, so K tiles are consumed earlier than V tiles).  The
+  // output staging tile is double-buffered unless a single buffer is what makes it fit.
+  int ob = 2;
+  auto fits = [&](int k, int v) { return (int)V.layout(k, v, pl->maxsub, ob).total <= kSmemLimit; };
+  int ks = 0, vs = 0;
+  for (int c = nsa::kMaxStages; c >= 1; --c)
+    if (fits(c, c)) { ks = vs = c; break; }
+  if (ks < 2) {
+    ob = 1;
     for (int c = nsa::kMaxStages; c >= 1; --c)
-      if (fits(c, c, a)) { s = c; break; }
-    if (s > ks && (a == 0 || ks < 2)) { ks = vs = s; alias = a; }
-  }
-  if (ks == 0) {
-    for (int a = 0; a <= 1 && ks == 0; ++a)
-      if (fits(2, 1, a)) { ks = 2; vs = 1; alias = a; }
+      if (fits(c, c)) { ks = vs = c; break; }
   }
   if (ks == 0) return fail(NSA_ERR_UNSUPPORTED, "tile does not fit in shared memory");
-  if (ks < nsa::kMaxStages && fits(ks + 1, vs, alias)) ++ks;
+  if (ks < nsa::kMaxStages && fits(ks + 1, vs)) ++ks;
   const char* env_ks = getenv("NSA_SEL_KSTAGES");
   const char* env_vs = getenv("NSA_SEL_VSTAGES");
   if (env_ks != nullptr || env_vs != nullptr) {
     const int eks = env_ks ? atoi(env_ks) : ks, evs = env_vs ? atoi(env_vs) : vs;
-    if (eks >= 1 && evs >= 1 && eks <= nsa::kMaxStages && evs <= nsa::kMaxStages) {
-      if (fits(eks, evs, alias)) {
-        ks = eks;
-        vs = evs;
-      } else if (fits(eks, evs, 1)) {
-        ks = eks;
-        vs = evs;
-        alias = 1;
-      }
+    if (eks >= 1 && evs >= 1 && eks <= nsa::kMaxStages && evs <= nsa::kMaxStages && fits(eks, evs)) {
+      ks = eks;
+      vs = evs;
     }
   }
   pl->KS = ks;
   pl->VS = vs;
-  pl->alias = alias;
-  pl->layout = V.layout(ks, vs, pl->maxsub, alias);
+  pl->out_bufs = ob;
+  pl->layout = V.layout(ks, vs, pl->maxsub, ob);
   int grid = sm_count > 0 ? sm_count : 148;
   if (d->max_ctas > 0 && d->max_ctas < grid) grid = d->max_ctas;
   if (grid > pl->n_units) grid = pl->n_units;
@@ -357,24 +354,28 @@ int launch(const nsa_sel_desc* d, nsa_stream_t stream) {
   p.off_out = pl.layout.off_out;
   p.off_tr = pl.layout.off_tr;
   p.off_alpha = pl.layout.off_alpha;
-  p.off_inv = pl.layout.off_inv;
+  p.off_fac = pl.layout.off_fac;
+  p.off_ml = pl.layout.off_ml;
   p.off_info = pl.layout.off_info;
   p.off_bar = pl.layout.off_bar;
-  p.stage_alias = pl.alias;
   p.debug_stall = (d->debug_flags & NSA_DEBUG_STALL) ? 1 : 0;
+  p.out_bufs = pl.out_bufs;
 
   {
     std::lock_guard<std::mutex> lk(g_dev.mu);
     const uint64_t bit = 1ull << pl.variant;
     if ((g_dev.attr_done[dev] & bit) == 0) {
-      cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(V.kernel),
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+      cudaFuncAttributes fa;
+      cudaError_t e = cudaFuncGetAttributes(&fa, reinterpret_cast<const void*>(V.kernel));
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncGetAttributes");
+      e = cudaFuncSetAttribute(reinterpret_cast<const void*>(V.kernel), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               kSmemLimit - (int)fa.sharedSizeBytes);
       if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
       g_dev.attr_done[dev] |= bit;
     }
   }
   void* args[] = {&tmQ, &tmK, &tmV, &tmO, &p};
-  cudaError_t e = cudaLaunchKernel(reinterpret_cast<const void*>(V.kernel), dim3(pl.grid), dim3(nsa::kThreads), args,
+  cudaError_t e = cudaLaunchKernel(reinterpret_cast<const void*>(V.kernel), dim3(pl.grid), dim3(V.threads), args,
                                    pl.layout.total, reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
   g_last_error[0] = '\0';

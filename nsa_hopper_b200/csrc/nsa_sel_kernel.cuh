@@ -10,22 +10,29 @@
 // How (B200-first design, not a translation of the Hopper kernels):
 //  * Persistent CTAs (one per SM) walk work units u = (b*Hkv+kvh, qb, part) in
 //    KV-head-major order, so all SMs sweep the tokens of one KV head together and the
-//    gathered K/V blocks of that head are re-read from L2 rather than HBM.  K/V loads
-//    carry an L2 evict_last hint, the streaming Q loads evict_first.
-//  * Warp 0 (loader) turns a unit's selection row into a list of 64-key sub-blocks
-//    (dedupe, padding, causal and range clipping) in a shared-memory "info" ring and issues
-//    TMA tensor loads: the unit's Q tile and, per chunk of two sub-blocks (128 keys), a K
-//    tile and a V tile into two mbarrier-driven rings.
-//  * Warp 1 (MMA) issues tcgen05 UMMAs from one thread in swap-AB form so the 128 keys of
-//    a chunk are the M=128 dimension and the G*BQ query rows are N (16..128):
+//    gathered K/V blocks of that head are re-read from L2 rather than HBM.  K/V loads carry
+//    an L2 evict_last hint, the streaming Q loads evict_first.
+//  * Loader warp: turns a unit's selection row into a list of 64-key sub-blocks (dedupe,
+//    padding, causal and range clipping) in a shared-memory "info" ring and issues TMA tensor
+//    loads: the unit's Q tile and, per chunk of two sub-blocks (128 keys), a K tile and a V
+//    tile into two mbarrier-driven rings.
+//  * MMA warp: one thread issues tcgen05 UMMAs in swap-AB form, so the 128 keys of a chunk
+//    are the M=128 dimension and the G*BQ query rows of the unit are N (16..64):
 //        S^T[keys x rows]  = K_chunk[keys x d_qk] . Q^T          (A K-major, B K-major)
 //        O^T[d_v x rows]  += V_chunk^T[d_v x keys] . P^T          (A MN-major, B K-major)
-//    S^T and O^T accumulate in TMEM (S double-buffered, O double-buffered per unit).
-//  * Warps 2-5 (softmax warpgroup) read S^T from TMEM, transpose it through shared memory
-//    so each thread owns 16 keys of one query row, mask, do an exp2 online softmax with a
-//    warp-shuffle row max/sum and lazy O rescaling (only when the running max grows by
-//    more than 2^8), write P^T as bf16 in the UMMA K-major SW128 layout, and finally
-//    normalise O^T, write LSE and store O with a TMA tensor store.
+//    It polls its barriers and issues a score MMA as soon as a K tile and one of four TMEM
+//    score buffers are free (running ahead of the softmax) and a PV MMA as soon as its P tile
+//    is ready.
+//  * NWG softmax warpgroups (1 or 2): chunk g of the stream belongs to group g % NWG, which
+//    keeps its own online-softmax state and its own O^T accumulator in TMEM (a split over the
+//    unit's keys, merged by the epilogue).  Per chunk a group reads S^T from TMEM, transposes
+//    it through shared memory so each thread owns NCOL keys of one query row, masks, runs an
+//    exp2 online softmax with a warp-shuffle row max and lazy O rescaling (only when the
+//    running max grows by more than 2^8), and writes P^T as bf16 in the UMMA K-major SW128
+//    layout.
+//  * Epilogue warpgroup: merges the groups' partial results (O, running max, sum), writes
+//    the fp32 log-sum-exp and stores O (bf16 or fp32) with TMA tensor stores, overlapping
+//    the softmax of the next unit.
 //
 // Every mbarrier wait is bounded by %globaltimer; a wait that runs out sets an error bit,
 // all roles stop, in-flight TMA loads/stores and UMMAs are drained and TMEM is freed.
@@ -37,18 +44,26 @@
 
 namespace nsa {
 
-constexpr int kSub = 64;         // keys per sub-block (one TMA box of rows)
-constexpr int kChunk = 128;      // keys per chunk = M of the UMMAs
-constexpr int kInfoSlots = 4;    // depth of the unit-info ring
-constexpr int kInfoHdr = 16;     // ints of header per info slot
-constexpr int kMaxStages = 8;    // upper bound on K and V ring depth
-constexpr int kThreads = 192;    // loader warp + MMA warp + 4 softmax warps
-constexpr int kLoaderWarp = 0;
-constexpr int kMmaWarp = 1;
-constexpr int kSoftmaxWarp0 = 2;
-constexpr uint32_t kWgBar = 1;   // named barrier of the softmax warpgroup
+constexpr int kSub = 64;          // keys per sub-block (one TMA box of rows)
+constexpr int kChunk = 128;       // keys per chunk = M of the UMMAs
+constexpr int kInfoSlots = 4;     // depth of the unit-info ring
+constexpr int kInfoHdr = 16;      // ints of header per info slot
+constexpr int kMaxStages = 8;     // upper bound on K and V ring depth
+constexpr int kSSlots = 4;        // TMEM score buffers (MMA look-ahead)
+constexpr int kQSlots = 3;        // Q tile ring (the loader stages one unit ahead)
+constexpr int kLoaderWarp = 0;    // unit info, Q tiles and K tiles
+constexpr int kMmaWarp = 1;       // score MMAs; owns the TMEM allocation
+constexpr int kEpiWarp0 = 2;      // warps 2..5: epilogue
+constexpr int kSoftWarp0 = 6;     // warps 6..6+4*NWG-1: softmax warpgroups; then the V loader and
+                                  // the PV MMA warp
+constexpr uint32_t kEpiBar = 1;   // named barrier of the epilogue warpgroup
+constexpr uint32_t kWgBar0 = 2;   // named barrier of softmax warpgroup w = kWgBar0 + w
 constexpr float kRescaleLog2 = 8.0f;
 constexpr int kDevErrTimeout = 1;
+
+__host__ __device__ constexpr int vloader_warp(int nwg) { return kSoftWarp0 + 4 * nwg; }
+__host__ __device__ constexpr int pv_warp(int nwg) { return kSoftWarp0 + 4 * nwg + 1; }
+__host__ __device__ constexpr int threads_for(int nwg) { return 32 * (pv_warp(nwg) + 1); }
 
 // Info-slot header fields.
 enum : int { kInfNsub = 0, kInfT0, kInfNtok, kInfKend, kInfB, kInfKvh, kInfBkv, kInfSeq0, kInfRef };
@@ -64,18 +79,27 @@ struct Params {
   int n_units, maxsub, KS, VS;
   float scale_log2;
   unsigned long long timeout_ns;
-  uint32_t off_k, off_v, off_q, off_p, off_out, off_tr, off_alpha, off_inv, off_info, off_bar;
-  int stage_alias;  // 1: the output staging tile lives in the transpose buffer (single buffer)
+  uint32_t off_k, off_v, off_q, off_p, off_out, off_tr, off_alpha, off_fac, off_ml, off_info, off_bar;
   int debug_stall;  // 1: the MMA warp first waits on a barrier nothing arrives on (error-path test)
+  int out_bufs;     // output staging tiles (2: double buffer; 1 when shared memory is tight)
 };
+
+// P tiles: two buffers.  With two softmax groups, group w always uses buffer w; with one
+// group, its k-th chunk uses buffer k & 1.  The (k)-th use of a buffer is its phase index.
+template <int NWG>
+__device__ __forceinline__ int pslot_of(int wg, uint32_t k) { return NWG == 2 ? wg : (int)(k & 1u); }
+template <int NWG>
+__device__ __forceinline__ uint32_t pphase_of(uint32_t k) { return NWG == 2 ? k : (k >> 1); }
 
 struct SmemBars {
   uint64_t info_full[kInfoSlots], info_empty[kInfoSlots];
-  uint64_t q_full[2], q_empty[2];
+  uint64_t q_full[kQSlots], q_empty[kQSlots];
   uint64_t k_full[kMaxStages], k_empty[kMaxStages];
   uint64_t v_full[kMaxStages], v_empty[kMaxStages];
-  uint64_t s_full[2], p_full[2], pv_done[2], o_empty[2];
-  uint64_t drain;
+  uint64_t s_full[kSSlots], s_empty[kSSlots];
+  uint64_t p_full[2], pv_done[2];
+  uint64_t o_full[2], wg_done[2], o_empty[2];
+  uint64_t drain_s, drain_pv;
   uint64_t stall;  // never arrived on; only the debug_stall path waits on it
   uint32_t tmem_base;
   int abort_flag;
@@ -88,13 +112,15 @@ __host__ __device__ constexpr int ceil_pow2_32(int x) {
 }
 __host__ __device__ constexpr uint32_t align_up(uint32_t x, uint32_t a) { return (x + a - 1) / a * a; }
 
-template <int DQK_, int DV_, int NCOL_, typename OutT_>
+template <int DQK_, int DV_, int NCOL_, typename OutT_, int NWG_>
 struct Cfg {
-  static constexpr int DQK = DQK_, DV = DV_, NCOL = NCOL_;
+  static constexpr int DQK = DQK_, DV = DV_, NCOL = NCOL_, NWG = NWG_;
   using OutT = OutT_;
   static_assert(DQK % 64 == 0 && DQK >= 64 && DQK <= 256, "d_qk must be 64..256 in steps of 64");
   static_assert(DV == 64 || DV == 128, "d_v must be 64 or 128");
   static_assert(NCOL == 16 || NCOL == 32 || NCOL == 64, "N must be 16/32/64");
+  static_assert(NWG == 1 || NWG == 2, "one or two softmax warpgroups");
+  static constexpr int kThreads = threads_for(NWG);
   static constexpr int kDvPad = DV < 128 ? 128 : DV;       // PV runs M=128; pad V tiles to 128 rows of d
   static constexpr int kBox = kSub * 128;                   // 64 rows x 128 B = 8 KB TMA box
   static constexpr int kKChunkStride = 2 * kBox;            // one 64-wide d slice of a 128-key K tile
@@ -111,37 +137,33 @@ struct Cfg {
   static constexpr int kTrBytes = NCOL * kTRS * 4;
   static constexpr int kOutChunkElems = NCOL * 64;
   static constexpr int kOutBytes = (DV / 64) * kOutChunkElems * (int)sizeof(OutT);
-  static constexpr int kTmemCols = ceil_pow2_32(4 * NCOL);
+  static constexpr int kTmemS = 0;                          // score buffers: kSSlots x NCOL columns
+  static constexpr int kTmemO = kSSlots * NCOL;             // O^T accumulators: [wg][unit parity] x NCOL
+  static constexpr int kTmemCols = ceil_pow2_32((kSSlots + 2 * NWG) * NCOL);
   static constexpr uint32_t kIdescS = ptx::idesc_bf16_f32(128, NCOL, false, false);
   static constexpr uint32_t kIdescPV = ptx::idesc_bf16_f32(128, NCOL, true, false);
 };
 
 // Shared-memory layout (byte offsets from a 1024-aligned base); identical on host and device.
 struct SmemLayout {
-  uint32_t off_k, off_v, off_q, off_p, off_out, off_tr, off_alpha, off_inv, off_info, off_bar, total;
+  uint32_t off_k, off_v, off_q, off_p, off_out, off_tr, off_alpha, off_fac, off_ml, off_info, off_bar, total;
 };
-// With `alias`, the (single) output staging tile reuses the transpose buffer, which is idle
-// between a unit's last chunk and the next unit's first chunk.
 template <class C>
-__host__ __device__ inline SmemLayout smem_layout(int KS, int VS, int maxsub, int alias) {
-  static_assert(C::kOutBytes <= C::kTrBytes, "staging tile must fit in the transpose buffer");
+__host__ __device__ inline SmemLayout smem_layout(int KS, int VS, int maxsub, int out_bufs) {
   SmemLayout s{};
   uint32_t o = 0;
   s.off_k = o; o += (uint32_t)KS * C::kKStage;
   s.off_v = o; o += (uint32_t)VS * C::kVStage;
-  s.off_q = o; o += 2u * C::kQBytes;
+  s.off_q = o; o += (uint32_t)kQSlots * C::kQBytes;
   o = align_up(o, 1024);
   s.off_p = o; o += 2u * C::kPBytes;
-  o = align_up(o, 1024);
-  s.off_tr = o; o += C::kTrBytes;
   o = align_up(o, 128);
-  if (alias) {
-    s.off_out = s.off_tr;
-  } else {
-    s.off_out = o; o += 2u * C::kOutBytes;
-  }
-  s.off_alpha = o; o += 4u * C::NCOL;
-  s.off_inv = o; o += 4u * C::NCOL;
+  s.off_out = o; o += (uint32_t)out_bufs * C::kOutBytes;
+  o = align_up(o, 16);
+  s.off_tr = o; o += (uint32_t)C::NWG * C::kTrBytes;
+  s.off_alpha = o; o += 4u * C::NWG * C::NCOL;
+  s.off_fac = o; o += 4u * C::NWG * C::NCOL;
+  s.off_ml = o; o += 8u * C::NWG * 2 * C::NCOL;  // [wg][unit parity][col] x {m, l}
   s.off_info = o; o += 4u * kInfoSlots * (kInfoHdr + maxsub);
   o = align_up(o, 16);
   s.off_bar = o; o += (uint32_t)sizeof(SmemBars);
@@ -156,6 +178,11 @@ struct Waiter {
   int32_t* err;
   unsigned long long timeout_ns;
 
+  __device__ __forceinline__ void raise() const {
+    *(volatile int*)abort_flag = 1;
+    if (err != nullptr) atomicOr(err, kDevErrTimeout);
+  }
+  __device__ __forceinline__ bool aborted() const { return *(volatile int*)abort_flag != 0; }
   __device__ __forceinline__ bool wait(uint64_t* bar, uint32_t parity) const {
     if (ptx::mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = ptx::globaltimer();
@@ -163,10 +190,9 @@ struct Waiter {
 #pragma unroll 1
       for (int i = 0; i < 32; ++i)
         if (ptx::mbar_try_wait(bar, parity)) return true;
-      if (*(volatile int*)abort_flag) return false;
+      if (aborted()) return false;
       if (ptx::globaltimer() - t0 > timeout_ns) {
-        *(volatile int*)abort_flag = 1;
-        if (err != nullptr) atomicOr(err, kDevErrTimeout);
+        raise();
         return false;
       }
     }
@@ -234,8 +260,14 @@ __device__ int build_unit_info(const Params& p, int u, int* inf, int lane) {
       const int j = base + lane;
       const int idx = (j < p.KSEL) ? __ldg(row + j) : -1;
       bool valid = idx >= 0 && idx < nblk && (seq0 + idx * p.LP) <= lim;
-      if (valid) {
-        for (int k2 = 0; k2 < j; ++k2)
+      // set semantics: drop repeats of an earlier entry (same 32-entry group by shuffle)
+#pragma unroll 8
+      for (int k2 = 0; k2 < 32; ++k2) {
+        const int other = __shfl_sync(0xffffffffu, idx, k2);
+        if (k2 < lane && other == idx) valid = false;
+      }
+      if (valid && base > 0) {  // earlier groups (KSEL > 32 only)
+        for (int k2 = 0; k2 < base; ++k2)
           if (__ldg(row + k2) == idx) { valid = false; break; }
       }
       const int bstart = valid ? seq0 + idx * p.LP : 0;
@@ -271,33 +303,38 @@ __device__ int build_unit_info(const Params& p, int u, int* inf, int lane) {
 }
 
 // ------------------------------------------------------------------------------------------
-// Loader warp: info ring + TMA loads of Q tiles and K/V chunk tiles.
+// Loader warp: info ring + TMA loads of Q and K tiles.  It runs one unit ahead for the unit
+// info and the Q tile (a three-deep Q ring), so the next unit's Q is already resident when the
+// score MMAs reach it; the unit's K chunk tiles follow in ring order.  V tiles have their own
+// loader warp, so neither ring waits for the other's slots.
 // ------------------------------------------------------------------------------------------
 template <class C>
 __device__ void loader_role(const CUtensorMap* tmQ, const CUtensorMap* tmK, const CUtensorMap* tmV,
                             const Params& p, uint8_t* smem, SmemBars* bars, const Waiter& w, int lane) {
   const uint64_t pol_kv = ptx::policy_evict_last();
   const uint64_t pol_q = ptx::policy_evict_first();
-  uint32_t ui = 0, qc = 0, kc = 0, vc = 0;  // units seen; Q, K and V tile loads issued
+  uint32_t qc = 0, kc = 0;  // Q and K tile loads issued
   bool ok = true;
-  for (int u = blockIdx.x; u < p.n_units; u += gridDim.x, ++ui) {
+
+  // Publish the info of the unit with sequence number `ui` (unit id u) and, if it has work,
+  // issue its Q tile.  Whole warp; returns false on abort.
+  auto stage_unit = [&](uint32_t ui, int u) -> bool {
     const int slot = ui % kInfoSlots;
     if (ui >= (uint32_t)kInfoSlots) {
       int r = 1;
       if (lane == 0) r = w.wait(&bars->info_empty[slot], ((ui / kInfoSlots) - 1) & 1) ? 1 : 0;
-      ok = __shfl_sync(0xffffffffu, r, 0) != 0;
-      if (!ok) break;
+      if (!__shfl_sync(0xffffffffu, r, 0)) return false;
     }
     int* inf = info_slot(p, smem, slot);
     const int nsub = build_unit_info(p, u, inf, lane);
     __syncwarp();
     if (lane == 0) ptx::mbar_arrive(&bars->info_full[slot]);
-    if (nsub == 0) continue;
+    if (nsub == 0) return true;
     int r = 1;
     if (lane == 0) {
-      const int t0 = inf[kInfT0], b = inf[kInfB], kvh = inf[kInfKvh], bkv = inf[kInfBkv];
-      const int qbuf = qc & 1;
-      if (qc >= 2 && !w.wait(&bars->q_empty[qbuf], ((qc >> 1) - 1) & 1)) {
+      const int t0 = inf[kInfT0], b = inf[kInfB], kvh = inf[kInfKvh];
+      const int qbuf = qc % kQSlots;
+      if (qc >= (uint32_t)kQSlots && !w.wait(&bars->q_empty[qbuf], ((qc / kQSlots) - 1) & 1)) {
         r = 0;
       } else {
         uint8_t* qdst = smem + p.off_q + qbuf * C::kQBytes;
@@ -306,6 +343,22 @@ __device__ void loader_role(const CUtensorMap* tmQ, const CUtensorMap* tmK, cons
           ptx::tma_load_4d(qdst + cc * C::kQChunk, tmQ, &bars->q_full[qbuf], cc * 64, t0, kvh * p.G, b, pol_q);
         ++qc;
       }
+    }
+    qc = __shfl_sync(0xffffffffu, qc, 0);
+    return __shfl_sync(0xffffffffu, r, 0) != 0;
+  };
+
+  uint32_t ui = 0;
+  int u = blockIdx.x;
+  if (u < p.n_units) ok = stage_unit(0, u);
+  for (; u < p.n_units && ok; u += gridDim.x, ++ui) {
+    // look ahead: the next unit's info and Q tile
+    if (u + (int)gridDim.x < p.n_units && !stage_unit(ui + 1, u + gridDim.x)) break;
+    const int* inf = info_slot(p, smem, ui % kInfoSlots);
+    const int nsub = inf[kInfNsub];
+    int r = 1;
+    if (lane == 0 && nsub > 0) {
+      const int bkv = inf[kInfBkv];
       const int nch = (nsub + 1) >> 1;
       for (int c = 0; c < nch && r; ++c) {
         const int nsc = min(2, nsub - 2 * c);
@@ -320,8 +373,43 @@ __device__ void loader_role(const CUtensorMap* tmQ, const CUtensorMap* tmK, cons
                              pol_kv);
         }
         ++kc;
+      }
+    }
+    ok = __shfl_sync(0xffffffffu, r, 0) != 0;
+    kc = __shfl_sync(0xffffffffu, kc, 0);
+  }
+  // Drain: wait until the most recent load issued into every ring stage has landed, so no
+  // TMA write can reach this CTA's shared memory after it exits.
+  if (lane == 0) {
+    for (uint32_t s = 0; s < (uint32_t)p.KS; ++s)
+      if (kc > s) w.wait_drain(&bars->k_full[s], ((s + ((kc - 1 - s) / p.KS) * p.KS) / p.KS) & 1);
+    for (uint32_t s = 0; s < (uint32_t)kQSlots; ++s)
+      if (qc > s) w.wait_drain(&bars->q_full[s], ((s + ((qc - 1 - s) / kQSlots) * kQSlots) / kQSlots) & 1);
+  }
+  __syncwarp();
+}
+
+// ------------------------------------------------------------------------------------------
+// V loader warp (lane 0): V chunk tiles into their ring, in the same chunk order.
+// ------------------------------------------------------------------------------------------
+template <class C>
+__device__ void vloader_role(const CUtensorMap* tmV, const Params& p, uint8_t* smem, SmemBars* bars,
+                             const Waiter& w, int lane) {
+  if (lane == 0) {
+    const uint64_t pol_kv = ptx::policy_evict_last();
+    uint32_t ui = 0, vc = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < p.n_units && ok; u += gridDim.x, ++ui) {
+      const int slot = ui % kInfoSlots;
+      if (!w.wait(&bars->info_full[slot], (ui / kInfoSlots) & 1)) break;
+      const int* inf = info_slot(p, smem, slot);
+      const int nsub = min(inf[kInfNsub], p.maxsub);
+      const int bkv = inf[kInfBkv];
+      const int nch = (nsub + 1) >> 1;
+      for (int c = 0; c < nch; ++c) {
+        const int nsc = min(2, nsub - 2 * c);
         const int vs = (int)(vc % (uint32_t)p.VS);
-        if (vc >= (uint32_t)p.VS && !w.wait(&bars->v_empty[vs], ((vc / p.VS) - 1) & 1)) { r = 0; break; }
+        if (vc >= (uint32_t)p.VS && !w.wait(&bars->v_empty[vs], ((vc / p.VS) - 1) & 1)) { ok = false; break; }
         uint8_t* vdst = smem + p.off_v + vs * C::kVStage;
         ptx::mbar_arrive_expect_tx(&bars->v_full[vs], (uint32_t)(nsc * kSub * C::DV * 2));
         for (int j = 0; j < nsc; ++j) {
@@ -331,193 +419,204 @@ __device__ void loader_role(const CUtensorMap* tmQ, const CUtensorMap* tmK, cons
         }
         ++vc;
       }
+      if (ok) ptx::mbar_arrive(&bars->info_empty[slot]);
     }
-    ok = __shfl_sync(0xffffffffu, r, 0) != 0;
-    qc = __shfl_sync(0xffffffffu, qc, 0);
-    kc = __shfl_sync(0xffffffffu, kc, 0);
-    vc = __shfl_sync(0xffffffffu, vc, 0);
-    if (!ok) break;
-  }
-  // Drain: wait until the most recent load issued into every ring stage has landed, so no
-  // TMA write can reach this CTA's shared memory after it exits.
-  if (lane == 0) {
-    for (uint32_t s = 0; s < (uint32_t)p.KS; ++s)
-      if (kc > s) w.wait_drain(&bars->k_full[s], ((s + ((kc - 1 - s) / p.KS) * p.KS) / p.KS) & 1);
+    // Drain: the most recent load of every stage has landed.
     for (uint32_t s = 0; s < (uint32_t)p.VS; ++s)
       if (vc > s) w.wait_drain(&bars->v_full[s], ((s + ((vc - 1 - s) / p.VS) * p.VS) / p.VS) & 1);
-    for (uint32_t s = 0; s < 2; ++s)
-      if (qc > s) w.wait_drain(&bars->q_full[s], ((s + ((qc - 1 - s) / 2) * 2) / 2) & 1);
   }
   __syncwarp();
 }
 
 // ------------------------------------------------------------------------------------------
-// MMA warp (lane 0 issues): S_g = K_g . Q^T, then PV_{g-1}, keeping one chunk of slack so
-// the softmax of chunk g-1 overlaps the score MMA of chunk g.
+// MMA issue.  Two warps each issue one stream from one thread, in ring order, with blocking
+// (bounded) waits:
+//   score warp: S_g = K_g . Q^T into TMEM score buffer g % 4 as soon as K_g has landed and the
+//               softmax has read the buffer's previous chunk (so it runs ahead of the softmax);
+//   PV warp:    O^T += V_g^T . P_g^T into the owning group's accumulator as soon as P_g and V_g
+//               are ready.
+// Shared-memory descriptors are built once per tile; each 16-wide K step adds a constant.
 // ------------------------------------------------------------------------------------------
-struct PendPV {
-  int valid, g, obuf, ne, first, nsc, vc;
-};
+__device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t byte_off) { return d + (uint64_t)(byte_off >> 4); }
 
 template <class C>
-__device__ bool issue_pv(const PendPV& pd, const Params& p, uint8_t* smem, SmemBars* bars, const Waiter& w,
-                         uint32_t tmem, long long& t_wait) {
-  if (!w.wait(&bars->p_full[pd.g & 1], (pd.g >> 1) & 1)) return false;
-  if (pd.first && pd.ne >= 2 && !w.wait(&bars->o_empty[pd.obuf], ((pd.ne >> 1) - 1) & 1)) return false;
-  const int vs = pd.vc % p.VS;
-  const long long t0 = clock64();
-  if (!w.wait(&bars->v_full[vs], (pd.vc / p.VS) & 1)) return false;
-  t_wait += clock64() - t0;
-  ptx::tc_fence_after();
-  const uint32_t vaddr = ptx::smem_u32(smem + p.off_v + vs * C::kVStage);
-  const uint32_t paddr = ptx::smem_u32(smem + p.off_p + (pd.g & 1) * C::kPBytes);
-  const uint32_t dO = tmem + 2 * C::NCOL + pd.obuf * C::NCOL;
-  for (int j = 0; j < pd.nsc * 4; ++j) {
-    const int sb = j >> 2, kk = j & 3;
-    const uint64_t a = ptx::sdesc_sw128(vaddr + sb * C::kVSub + kk * 2048, C::kBox, 1024);
-    const uint64_t bp = ptx::sdesc_sw128(paddr + sb * C::kPSub + kk * 32, 16, 1024);
-    ptx::umma_bf16(dO, a, bp, C::kIdescPV, (pd.first && j == 0) ? 0u : 1u);
-  }
-  ptx::umma_commit(&bars->v_empty[vs]);
-  ptx::umma_commit(&bars->pv_done[pd.g & 1]);
-  return true;
-}
-
-template <class C>
-__device__ void mma_role(const Params& p, uint8_t* smem, SmemBars* bars, const Waiter& w, uint32_t tmem, int lane) {
+__device__ void mma_s_role(const Params& p, uint8_t* smem, SmemBars* bars, const Waiter& w, uint32_t tmem, int lane) {
   if (lane == 0) {
-    uint32_t ui = 0, ne = 0, kc = 0, vc = 0, g = 0;
-    PendPV pend{0, 0, 0, 0, 0, 0, 0};
     bool ok = true;
-    long long t_wait = 0;
     // Error-path test hook: a bounded wait that can only end by running out of time.
     if (p.debug_stall) ok = w.wait(&bars->stall, 0);
+    uint32_t g = 0, kc = 0, ui = 0, ne = 0;
+    const uint32_t k_base = ptx::smem_u32(smem + p.off_k);
+    const uint32_t q_base = ptx::smem_u32(smem + p.off_q);
     for (int u = blockIdx.x; u < p.n_units && ok; u += gridDim.x, ++ui) {
       const int slot = ui % kInfoSlots;
-      if (!w.wait(&bars->info_full[slot], (ui / kInfoSlots) & 1)) { ok = false; break; }
+      if (!w.wait(&bars->info_full[slot], (ui / kInfoSlots) & 1)) break;
       const int* inf = info_slot(p, smem, slot);
       const int nsub = min(inf[kInfNsub], p.maxsub);
       const int ref = inf[kInfRef];
       const int nch = (nsub + 1) >> 1;
-      if (nch == 0) {
-        // Nothing to overlap with: retire the previous unit's last PV now, so its epilogue
-        // (and the info slot it holds) never waits on units further ahead.
-        if (pend.valid) {
-          if (!issue_pv<C>(pend, p, smem, bars, w, tmem, t_wait)) { ok = false; break; }
-          pend.valid = 0;
-        }
-        ptx::mbar_arrive(&bars->info_empty[slot]);
-        continue;
-      }
-      const long long t_unit0 = clock64();
-      t_wait = 0;
-      const int qbuf = ne & 1;
-      if (!w.wait(&bars->q_full[qbuf], (ne >> 1) & 1)) { ok = false; break; }
-      const uint32_t qaddr = ptx::smem_u32(smem + p.off_q + qbuf * C::kQBytes);
-      for (int c = 0; c < nch; ++c) {
-        const int nsc = min(2, nsub - 2 * c);
-        const int ks = kc % p.KS;
-        const long long tw = clock64();
-        if (!w.wait(&bars->k_full[ks], (kc / p.KS) & 1)) { ok = false; break; }
-        t_wait += clock64() - tw;
-        ptx::tc_fence_after();
-        const uint32_t kaddr = ptx::smem_u32(smem + p.off_k + ks * C::kKStage);
-        const uint32_t dS = tmem + (g & 1) * C::NCOL;
+      if (nch > 0) {
+        const int qs = ne % kQSlots;
+        long long t_wait = 0;
+        if (!w.wait(&bars->q_full[qs], (ne / kQSlots) & 1)) break;
+        const uint64_t bq0 = ptx::sdesc_sw128(q_base + qs * C::kQBytes, 16, 1024);
+        for (int c = 0; c < nch; ++c, ++g, ++kc) {
+          const int sslot = g % kSSlots;
+          const int ks = kc % p.KS;
+          if (g >= (uint32_t)kSSlots && !w.wait(&bars->s_empty[sslot], ((g / kSSlots) - 1) & 1)) { ok = false; break; }
+          const long long t0 = clock64();
+          if (!w.wait(&bars->k_full[ks], (kc / p.KS) & 1)) { ok = false; break; }
+          t_wait += clock64() - t0;
+          ptx::tc_fence_after();
+          const uint64_t a0 = ptx::sdesc_sw128(k_base + ks * C::kKStage, 16, 1024);
+          const uint32_t dS = tmem + C::kTmemS + sslot * C::NCOL;
 #pragma unroll
-        for (int j = 0; j < C::DQK / 16; ++j) {
-          const int cc = j >> 2, kk = j & 3;
-          const uint64_t a = ptx::sdesc_sw128(kaddr + cc * C::kKChunkStride + kk * 32, 16, 1024);
-          const uint64_t bq = ptx::sdesc_sw128(qaddr + cc * C::kQChunk + kk * 32, 16, 1024);
-          ptx::umma_bf16(dS, a, bq, C::kIdescS, j > 0 ? 1u : 0u);
+          for (int j = 0; j < C::DQK / 16; ++j) {
+            const uint32_t ca = (j >> 2) * C::kKChunkStride + (j & 3) * 32;
+            const uint32_t cb = (j >> 2) * C::kQChunk + (j & 3) * 32;
+            ptx::umma_bf16(dS, desc_add(a0, ca), desc_add(bq0, cb), C::kIdescS, j > 0 ? 1u : 0u);
+          }
+          ptx::umma_commit(&bars->k_empty[ks]);
+          ptx::umma_commit(&bars->s_full[sslot]);
         }
-        ptx::umma_commit(&bars->k_empty[ks]);
-        ptx::umma_commit(&bars->s_full[g & 1]);
-        if (c == nch - 1) ptx::umma_commit(&bars->q_empty[qbuf]);
-        ++kc;
-        if (pend.valid && !issue_pv<C>(pend, p, smem, bars, w, tmem, t_wait)) { ok = false; break; }
-        pend = PendPV{1, (int)g, (int)(ne & 1), (int)ne, c == 0 ? 1 : 0, nsc, (int)vc};
-        ++vc;
-        ++g;
+        if (!ok) break;
+        ptx::umma_commit(&bars->q_empty[qs]);
+        if (p.cyc != nullptr) atomicAdd(reinterpret_cast<unsigned long long*>(p.cyc + 2 * (size_t)ref),
+                                        (unsigned long long)t_wait);
+        ++ne;
       }
-      if (!ok) break;
       ptx::mbar_arrive(&bars->info_empty[slot]);
-      ++ne;
-      if (p.cyc != nullptr) {
-        const long long tot = clock64() - t_unit0;
-        atomicAdd(reinterpret_cast<unsigned long long*>(p.cyc + 2 * (size_t)ref), (unsigned long long)t_wait);
-        atomicAdd(reinterpret_cast<unsigned long long*>(p.cyc + 2 * (size_t)ref + 1),
-                  (unsigned long long)(tot > t_wait ? tot - t_wait : 0));
-      }
     }
-    if (ok && pend.valid) issue_pv<C>(pend, p, smem, bars, w, tmem, t_wait);
     // Drain: every UMMA issued by this thread completes before TMEM is released.
-    ptx::umma_commit(&bars->drain);
-    w.wait_drain(&bars->drain, 0);
+    ptx::umma_commit(&bars->drain_s);
+    w.wait_drain(&bars->drain_s, 0);
+  }
+  __syncwarp();
+}
+
+template <class C>
+__device__ void mma_pv_role(const Params& p, uint8_t* smem, SmemBars* bars, const Waiter& w, uint32_t tmem,
+                            int lane) {
+  if (lane == 0) {
+    bool ok = true;
+    uint32_t vc = 0, ui = 0, ne = 0;
+    uint32_t kc0 = 0, kc1 = 0;  // chunks so far of softmax group 0 / 1
+    const uint32_t v_base = ptx::smem_u32(smem + p.off_v);
+    const uint32_t p_base = ptx::smem_u32(smem + p.off_p);
+    for (int u = blockIdx.x; u < p.n_units && ok; u += gridDim.x, ++ui) {
+      const int slot = ui % kInfoSlots;
+      if (!w.wait(&bars->info_full[slot], (ui / kInfoSlots) & 1)) break;
+      const int* inf = info_slot(p, smem, slot);
+      const int nsub = min(inf[kInfNsub], p.maxsub);
+      const int ref = inf[kInfRef];
+      const int nch = (nsub + 1) >> 1;
+      if (nch > 0) {
+        const long long t_unit0 = clock64();
+        long long t_wait = 0;
+        for (int c = 0; c < nch; ++c, ++vc) {
+          const int wg = c % C::NWG;
+          const uint32_t k = wg ? kc1++ : kc0++;
+          const int ps = pslot_of<C::NWG>(wg, k);
+          const int nsc = min(2, nsub - 2 * c);
+          const int vs = vc % p.VS;
+          const bool first = c < C::NWG;
+          if (!w.wait(&bars->p_full[ps], pphase_of<C::NWG>(k) & 1)) { ok = false; break; }
+          if (first && ne >= 2 && !w.wait(&bars->o_empty[ne & 1], ((ne >> 1) - 1) & 1)) { ok = false; break; }
+          const long long t0 = clock64();
+          if (!w.wait(&bars->v_full[vs], (vc / p.VS) & 1)) { ok = false; break; }
+          t_wait += clock64() - t0;
+          ptx::tc_fence_after();
+          const uint64_t a0 = ptx::sdesc_sw128(v_base + vs * C::kVStage, C::kBox, 1024);
+          const uint64_t b0 = ptx::sdesc_sw128(p_base + ps * C::kPBytes, 16, 1024);
+          const uint32_t dO = tmem + C::kTmemO + (wg * 2 + (ne & 1)) * C::NCOL;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            if (j < nsc * 4) {
+              const uint32_t ca = (j >> 2) * C::kVSub + (j & 3) * 2048;
+              const uint32_t cb = (j >> 2) * C::kPSub + (j & 3) * 32;
+              ptx::umma_bf16(dO, desc_add(a0, ca), desc_add(b0, cb), C::kIdescPV, (first && j == 0) ? 0u : 1u);
+            }
+          }
+          ptx::umma_commit(&bars->v_empty[vs]);
+          ptx::umma_commit(&bars->pv_done[ps]);
+        }
+        if (!ok) break;
+        ptx::umma_commit(&bars->o_full[ne & 1]);
+        if (p.cyc != nullptr) {
+          const long long tot = clock64() - t_unit0;
+          atomicAdd(reinterpret_cast<unsigned long long*>(p.cyc + 2 * (size_t)ref), (unsigned long long)t_wait);
+          atomicAdd(reinterpret_cast<unsigned long long*>(p.cyc + 2 * (size_t)ref + 1),
+                    (unsigned long long)(tot > t_wait ? tot - t_wait : 0));
+        }
+        ++ne;
+      }
+      ptx::mbar_arrive(&bars->info_empty[slot]);
+    }
+    ptx::umma_commit(&bars->drain_pv);
+    w.wait_drain(&bars->drain_pv, 0);
   }
   __syncwarp();
 }
 
 // ------------------------------------------------------------------------------------------
-// Softmax warpgroup.
+// Softmax warpgroup `wg` (128 threads): chunk c of every unit with c % NWG == wg.
 // ------------------------------------------------------------------------------------------
-template <typename T>
-__device__ __forceinline__ T to_out(float x);
-template <>
-__device__ __forceinline__ float to_out<float>(float x) { return x; }
-template <>
-__device__ __forceinline__ __nv_bfloat16 to_out<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
-
 template <class C>
-__device__ void softmax_role(const CUtensorMap* tmO, const Params& p, uint8_t* smem, SmemBars* bars,
-                             const Waiter& w, uint32_t tmem) {
-  constexpr int NCOL = C::NCOL, TPC = C::kTPC, KPT = C::kKPT;
-  using OutT = typename C::OutT;
-  const int i = threadIdx.x - kSoftmaxWarp0 * 32;  // 0..127 inside the warpgroup
+__device__ void softmax_role(const Params& p, uint8_t* smem, SmemBars* bars, const Waiter& w, uint32_t tmem,
+                             int wg) {
+  constexpr int NCOL = C::NCOL, TPC = C::kTPC, KPT = C::kKPT, NWG = C::NWG;
+  const uint32_t bar_id = kWgBar0 + wg;
+  const int i = threadIdx.x - (kSoftWarp0 + 4 * wg) * 32;  // 0..127 inside the warpgroup
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int quarter = warp & 3;                    // TMEM lane quarter this warp may access
   const int L = quarter * 32 + lane;               // TMEM lane (key of a chunk / d of O^T)
   const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
   const int col = i / TPC, kg = i - (i / TPC) * TPC;
-  float* tr = reinterpret_cast<float*>(smem + p.off_tr);
-  float* alpha_s = reinterpret_cast<float*>(smem + p.off_alpha);
-  float* inv_s = reinterpret_cast<float*>(smem + p.off_inv);
+  float* tr = reinterpret_cast<float*>(smem + p.off_tr + wg * C::kTrBytes);
+  float* alpha_s = reinterpret_cast<float*>(smem + p.off_alpha) + wg * NCOL;
+  float2* ml = reinterpret_cast<float2*>(smem + p.off_ml) + wg * 2 * NCOL;
   const float sl2 = p.scale_log2;
   const int nrows = p.G * p.BQs;
   const bool col_real = col < nrows;
-  const int col_g = col / p.BQs, col_i = col - (col / p.BQs) * p.BQs;
-  uint32_t ui = 0, ne = 0, g = 0, st = 0;
-  bool dead = false, quit = false;
+  const int col_i = col - (col / p.BQs) * p.BQs;
+  uint32_t ui = 0, ne = 0, g = 0, k = 0;  // k: chunks this group has processed
+  bool dead = false;
 
   for (int u = blockIdx.x; u < p.n_units; u += gridDim.x, ++ui) {
     const int slot = ui % kInfoSlots;
     dead |= !w.wait(&bars->info_full[slot], (ui / kInfoSlots) & 1);
-    if (p.stage_alias && i == 0) ptx::bulk_wait_read<0>();  // staging (= transpose buffer) is free
-    if (ptx::named_bar_or(kWgBar, 128, dead)) break;
+    if (ptx::named_bar_or(bar_id, 128, dead)) break;
     const int* inf = info_slot(p, smem, slot);
     const int nsub = min(inf[kInfNsub], p.maxsub);
-    const int t0 = inf[kInfT0], ntok = inf[kInfNtok], kend = inf[kInfKend];
-    const int b = inf[kInfB], kvh = inf[kInfKvh];
+    const int t0 = inf[kInfT0], kend = inf[kInfKend];
     const int nch = (nsub + 1) >> 1;
+    if (nch == 0) {
+      if (i == 0) ptx::mbar_arrive(&bars->info_empty[slot]);
+      continue;
+    }
     const int tcol = t0 + col_i;
-    const bool col_live = col_real && col_i < ntok;
-    const uint32_t obase = tmem + lane_addr + 2 * NCOL + (ne & 1) * NCOL;
+    const uint32_t obase = tmem + lane_addr + C::kTmemO + (wg * 2 + (ne & 1)) * NCOL;
     float m_run = -INFINITY, l_run = 0.f;
+    bool first = true, quit = false;
 
-    for (int c = 0; c < nch; ++c) {
-      dead |= !w.wait(&bars->s_full[g & 1], (g >> 1) & 1);
+    for (int c = wg; c < nch; c += NWG) {
+      const uint32_t gg = g + c;
+      const int sslot = gg % kSSlots;
+      dead |= !w.wait(&bars->s_full[sslot], (gg / kSSlots) & 1);
       ptx::tc_fence_after();
       {
-        const uint32_t saddr = tmem + lane_addr + (g & 1) * NCOL;
+        const uint32_t saddr = tmem + lane_addr + C::kTmemS + sslot * NCOL;
+        float v[NCOL];
 #pragma unroll
-        for (int h0 = 0; h0 < NCOL; h0 += 16) {
-          float v[16];
-          ptx::tmem_ld16(saddr + h0, v);
-          ptx::tmem_wait_ld();
+        for (int h0 = 0; h0 < NCOL; h0 += 16) ptx::tmem_ld16(saddr + h0, *reinterpret_cast<float(*)[16]>(&v[h0]));
+        ptx::tmem_wait_ld();
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&bars->s_empty[sslot]);  // score buffer may be rewritten
 #pragma unroll
-          for (int j = 0; j < 16; ++j) tr[(h0 + j) * C::kTRS + L] = v[j];
-        }
+        for (int j = 0; j < NCOL; ++j) tr[j * C::kTRS + L] = v[j];
       }
-      if (ptx::named_bar_or(kWgBar, 128, dead)) { quit = true; break; }
+      if (ptx::named_bar_or(bar_id, 128, dead)) { quit = true; break; }
 
       // This thread's keys of row `col`: key = 4*TPC*q4 + 4*kg + j.
       const int s0 = inf[kInfoHdr + 2 * c];
@@ -533,27 +632,29 @@ __device__ void softmax_role(const CUtensorMap* tmO, const Params& p, uint8_t* s
         sc[4 * q4 + 2] = x.z;
         sc[4 * q4 + 3] = x.w;
       }
-      float cmax = -INFINITY;
+      if (!full) {
 #pragma unroll
-      for (int q4 = 0; q4 < KPT / 4; ++q4) {
+        for (int q4 = 0; q4 < KPT / 4; ++q4) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int key = 4 * TPC * q4 + 4 * kg + j;
-          if (!full) {
+          for (int j = 0; j < 4; ++j) {
+            const int key = 4 * TPC * q4 + 4 * kg + j;
             const int sb = key >> 6;
             const int kpos = (sb ? s1 : s0) + (key & 63);
             const bool valid = (sb == 0 || has1) && kpos <= tcol && kpos < kend;
             if (!valid) sc[4 * q4 + j] = -INFINITY;
           }
-          cmax = fmaxf(cmax, sc[4 * q4 + j]);
         }
       }
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int q = 0; q < KPT; ++q) mx[q & 3] = fmaxf(mx[q & 3], sc[q]);
+      float cmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
 #pragma unroll
       for (int o = 1; o < TPC; o <<= 1) cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, o));
       const float cmax_x = cmax * sl2;
       float m_use = m_run, alpha = 1.f;
       bool need = false;
-      if (c == 0) {
+      if (first) {
         m_use = cmax_x;
       } else {
         const float m_cand = fmaxf(m_run, cmax_x);
@@ -564,10 +665,10 @@ __device__ void softmax_role(const CUtensorMap* tmO, const Params& p, uint8_t* s
         }
       }
       if (kg == 0) alpha_s[col] = alpha;
-      const bool any = ptx::named_bar_or(kWgBar, 128, need);
+      const bool any = ptx::named_bar_or(bar_id, 128, need);
       if (any) {
-        // Rescale O^T (lane L = d) by the per-row factors once the previous PV has landed.
-        dead |= !w.wait(&bars->pv_done[(g - 1) & 1], ((g - 1) >> 1) & 1);
+        // Rescale this group's O^T (lane L = d) once its previous PV (chunk k-1) has landed.
+        dead |= !w.wait(&bars->pv_done[pslot_of<NWG>(wg, k - 1)], pphase_of<NWG>(k - 1) & 1);
         ptx::tc_fence_after();
 #pragma unroll
         for (int h0 = 0; h0 < NCOL; h0 += 16) {
@@ -580,12 +681,14 @@ __device__ void softmax_role(const CUtensorMap* tmO, const Params& p, uint8_t* s
         }
         ptx::tmem_wait_st();
       }
-      // P buffer (g & 1) was read by PV_{g-2}.
-      if (g >= 2) dead |= !w.wait(&bars->pv_done[g & 1], ((g - 2) >> 1) & 1);
+      // The P buffer was last read by this group's PV of chunk k-1 (two groups) or k-2 (one).
+      const int ps = pslot_of<NWG>(wg, k);
+      const uint32_t pph = pphase_of<NWG>(k);
+      if (pph >= 1) dead |= !w.wait(&bars->pv_done[ps], (pph - 1) & 1);
 
       const float mref = (m_use == -INFINITY) ? 0.f : m_use;
       float lsum = 0.f;
-      uint8_t* pbuf = smem + p.off_p + (g & 1) * C::kPBytes;
+      uint8_t* pbuf = smem + p.off_p + ps * C::kPBytes;
 #pragma unroll
       for (int q4 = 0; q4 < KPT / 4; ++q4) {
         float pr[4];
@@ -608,65 +711,144 @@ __device__ void softmax_role(const CUtensorMap* tmO, const Params& p, uint8_t* s
       }
       l_run = l_run * alpha + lsum;
       m_run = m_use;
+      first = false;
       ptx::fence_proxy_async_smem();
       ptx::tc_fence_before();
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&bars->p_full[g & 1]);
-      ++g;
+      if (lane == 0) ptx::mbar_arrive(&bars->p_full[ps]);
+      ++k;
     }
     if (quit) break;
+    g += nch;
 
-    // ---- epilogue: normalise, LSE, O store
-    if (nch > 0) {
-      dead |= !w.wait(&bars->pv_done[(g - 1) & 1], ((g - 1) >> 1) & 1);
-      ptx::tc_fence_after();
-    }
+    // Publish this group's running max and sum for the epilogue's merge.  The slot of unit
+    // ne was last read by the epilogue for unit ne-2 (it arrives on o_empty after that).
+    if (ne >= 2) dead |= !w.wait(&bars->o_empty[ne & 1], ((ne >> 1) - 1) & 1);
     float lt = l_run;
 #pragma unroll
     for (int o = 1; o < TPC; o <<= 1) lt += __shfl_xor_sync(0xffffffffu, lt, o);
-    if (kg == 0) {
-      inv_s[col] = lt > 0.f ? 1.f / lt : 0.f;
-      if (col_live && p.lse != nullptr) {
-        const float lse = lt > 0.f ? (m_run + log2f(lt)) * 0.69314718055994530942f : -INFINITY;
-        p.lse[((size_t)b * p.Hq + (size_t)kvh * p.G + col_g) * p.T + tcol] = lse;
+    if (kg == 0) ml[(ne & 1) * NCOL + col] = make_float2(m_run, lt);
+    __syncwarp();
+    if (lane == 0) ptx::mbar_arrive(&bars->wg_done[ne & 1]);
+    if (i == 0) ptx::mbar_arrive(&bars->info_empty[slot]);
+    ++ne;
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// Epilogue warpgroup: merge the softmax groups' partial results, write LSE, store O.
+// ------------------------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ T to_out(float x);
+template <>
+__device__ __forceinline__ float to_out<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 to_out<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+
+template <class C>
+__device__ void epilogue_role(const CUtensorMap* tmO, const Params& p, uint8_t* smem, SmemBars* bars,
+                              const Waiter& w, uint32_t tmem) {
+  constexpr int NCOL = C::NCOL, NWG = C::NWG;
+  using OutT = typename C::OutT;
+  const int i = threadIdx.x - kEpiWarp0 * 32;  // 0..127
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int quarter = warp & 3;
+  const int L = quarter * 32 + lane;
+  const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+  float* fac = reinterpret_cast<float*>(smem + p.off_fac);  // [wg][col]: merge weight / sum
+  const float2* ml = reinterpret_cast<const float2*>(smem + p.off_ml);
+  const int nrows = p.G * p.BQs;
+  uint32_t ui = 0, ne = 0, st = 0;
+  bool dead = false;
+
+  for (int u = blockIdx.x; u < p.n_units; u += gridDim.x, ++ui) {
+    const int slot = ui % kInfoSlots;
+    dead |= !w.wait(&bars->info_full[slot], (ui / kInfoSlots) & 1);
+    if (ptx::named_bar_or(kEpiBar, 128, dead)) break;
+    const int* inf = info_slot(p, smem, slot);
+    const int nsub = min(inf[kInfNsub], p.maxsub);
+    const int t0 = inf[kInfT0], ntok = inf[kInfNtok], b = inf[kInfB], kvh = inf[kInfKvh];
+    const int nch = (nsub + 1) >> 1;
+    // group q took part iff the unit has a chunk c with c % NWG == q
+    bool part[NWG];
+#pragma unroll
+    for (int q = 0; q < NWG; ++q) part[q] = nch > q;
+    if (nch > 0) {
+      dead |= !w.wait(&bars->wg_done[ne & 1], (ne >> 1) & 1);
+      dead |= !w.wait(&bars->o_full[ne & 1], (ne >> 1) & 1);
+      ptx::tc_fence_after();
+    }
+    if (i < NCOL) {
+      // merge: O = sum_w O_w 2^(m_w - M) / sum_w l_w 2^(m_w - M)
+      float mw[NWG], lw[NWG], M = -INFINITY;
+#pragma unroll
+      for (int q = 0; q < NWG; ++q) {
+        const float2 v = (nch > 0 && part[q]) ? ml[(q * 2 + (ne & 1)) * NCOL + i] : make_float2(-INFINITY, 0.f);
+        mw[q] = v.x;
+        lw[q] = v.y;
+        M = fmaxf(M, v.x);
+      }
+      float a[NWG], Ls = 0.f;
+#pragma unroll
+      for (int q = 0; q < NWG; ++q) {
+        a[q] = (mw[q] == -INFINITY || lw[q] == 0.f) ? 0.f : ptx::ex2(mw[q] - M);
+        Ls += lw[q] * a[q];
+      }
+      const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
+#pragma unroll
+      for (int q = 0; q < NWG; ++q) fac[q * NCOL + i] = a[q] * inv;
+      const int cg = i / p.BQs, ci = i - (i / p.BQs) * p.BQs;
+      if (i < nrows && ci < ntok && p.lse != nullptr) {
+        const float lse = Ls > 0.f ? (M + log2f(Ls)) * 0.69314718055994530942f : -INFINITY;
+        p.lse[((size_t)b * p.Hq + (size_t)kvh * p.G + cg) * p.T + t0 + ci] = lse;
       }
     }
+    if (ntok > 0 && i == 0) {  // the store that last read this staging buffer is done
+      if (p.out_bufs == 2) ptx::bulk_wait_read<1>(); else ptx::bulk_wait_read<0>();
+    }
+    ptx::named_bar_sync(kEpiBar, 128);
     if (ntok > 0) {
-      if (i == 0) ptx::bulk_wait_read<1>();  // the TMA store that last read this staging buffer is done
-      ptx::named_bar_sync(kWgBar, 128);
-      OutT* stg = reinterpret_cast<OutT*>(smem + p.off_out + (p.stage_alias ? 0u : (st & 1) * C::kOutBytes));
+      OutT* stg = reinterpret_cast<OutT*>(smem + p.off_out + (p.out_bufs == 2 ? (st & 1) : 0u) * C::kOutBytes);
       OutT* dst = stg + (L >> 6) * C::kOutChunkElems + (L & 63);
 #pragma unroll
       for (int h0 = 0; h0 < NCOL; h0 += 16) {
-        float t16[16];
-        if (nch > 0) {
-          ptx::tmem_ld16(obase + h0, t16);
-          ptx::tmem_wait_ld();
-        } else {
+        float acc[16];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) t16[j] = 0.f;
+        for (int j = 0; j < 16; ++j) acc[j] = 0.f;
+#pragma unroll
+        for (int q = 0; q < NWG; ++q) {
+          if (part[q]) {
+            float t16[16];
+            ptx::tmem_ld16(tmem + lane_addr + C::kTmemO + (q * 2 + (ne & 1)) * NCOL + h0, t16);
+            ptx::tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) acc[j] = fmaf(t16[j], fac[q * NCOL + h0 + j], acc[j]);
+          }
         }
         if (L < C::DV) {
 #pragma unroll
           for (int j = 0; j < 16; ++j)
-            if (h0 + j < nrows) dst[(h0 + j) * 64] = to_out<OutT>(t16[j] * inv_s[h0 + j]);
+            if (h0 + j < nrows) dst[(h0 + j) * 64] = to_out<OutT>(acc[j]);
         }
       }
-      if (nch > 0) {
-        ptx::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&bars->o_empty[ne & 1]);
-      }
-      ptx::fence_proxy_async_smem();
-      ptx::named_bar_sync(kWgBar, 128);
-      if (i == 0) {
+    }
+    if (nch > 0) {
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&bars->o_empty[ne & 1]);  // O^T buffers and ml slot are free
+    }
+    ptx::fence_proxy_async_smem();
+    ptx::named_bar_sync(kEpiBar, 128);
+    if (i == 0) {
+      if (ntok > 0) {
+        OutT* stg = reinterpret_cast<OutT*>(smem + p.off_out + (p.out_bufs == 2 ? (st & 1) : 0u) * C::kOutBytes);
         for (int dc = 0; dc < C::DV / 64; ++dc)
           ptx::tma_store_4d(tmO, stg + dc * C::kOutChunkElems, dc * 64, t0, kvh * p.G, b);
         ptx::bulk_commit();
       }
-      ++st;
+      ptx::mbar_arrive(&bars->info_empty[slot]);
     }
-    if (i == 0) ptx::mbar_arrive(&bars->info_empty[slot]);
+    if (ntok > 0) ++st;
     if (nch > 0) ++ne;
   }
   if (i == 0) ptx::bulk_wait<0>();
@@ -674,7 +856,7 @@ __device__ void softmax_role(const CUtensorMap* tmO, const Params& p, uint8_t* s
 
 // ------------------------------------------------------------------------------------------
 template <class C>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(C::kThreads, 1)
     nsa_sel_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
                        const __grid_constant__ Params p) {
@@ -685,14 +867,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kInfoSlots; ++s) {
       ptx::mbar_init(&bars->info_full[s], 1);
-      ptx::mbar_init(&bars->info_empty[s], 2);
+      ptx::mbar_init(&bars->info_empty[s], 4 + C::NWG);  // 2 MMA warps, V loader, epilogue, each softmax group
     }
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kSSlots; ++s) {
+      ptx::mbar_init(&bars->s_full[s], 1);
+      ptx::mbar_init(&bars->s_empty[s], 4);
+    }
+    for (int s = 0; s < kQSlots; ++s) {
       ptx::mbar_init(&bars->q_full[s], 1);
       ptx::mbar_init(&bars->q_empty[s], 1);
-      ptx::mbar_init(&bars->s_full[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
       ptx::mbar_init(&bars->p_full[s], 4);
       ptx::mbar_init(&bars->pv_done[s], 1);
+      ptx::mbar_init(&bars->o_full[s], 1);
+      ptx::mbar_init(&bars->wg_done[s], 4 * C::NWG);
       ptx::mbar_init(&bars->o_empty[s], 4);
     }
     for (int s = 0; s < kMaxStages; ++s) {
@@ -701,13 +890,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_init(&bars->v_full[s], 1);
       ptx::mbar_init(&bars->v_empty[s], 1);
     }
-    ptx::mbar_init(&bars->drain, 1);
+    ptx::mbar_init(&bars->drain_s, 1);
+    ptx::mbar_init(&bars->drain_pv, 1);
     ptx::mbar_init(&bars->stall, 1);
     bars->abort_flag = 0;
     ptx::fence_mbar_init();
   }
   // Rows of the Q tiles beyond G*BQs are never written by TMA and must read as zero.
-  for (int idx = threadIdx.x; idx < 2 * C::kQBytes / 16; idx += kThreads)
+  for (int idx = threadIdx.x; idx < kQSlots * C::kQBytes / 16; idx += C::kThreads)
     reinterpret_cast<uint4*>(smem + p.off_q)[idx] = make_uint4(0u, 0u, 0u, 0u);
   ptx::fence_proxy_async_smem();
   if (warp == kLoaderWarp && lane == 0) {
@@ -729,9 +919,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == kLoaderWarp) {
     loader_role<C>(&tmQ, &tmK, &tmV, p, smem, bars, w, lane);
   } else if (warp == kMmaWarp) {
-    mma_role<C>(p, smem, bars, w, tmem, lane);
+    mma_s_role<C>(p, smem, bars, w, tmem, lane);
+  } else if (warp < kSoftWarp0) {
+    epilogue_role<C>(&tmO, p, smem, bars, w, tmem);
+  } else if (warp < vloader_warp(C::NWG)) {
+    softmax_role<C>(p, smem, bars, w, tmem, (warp - kSoftWarp0) >> 2);
+  } else if (warp == vloader_warp(C::NWG)) {
+    vloader_role<C>(&tmV, p, smem, bars, w, lane);
   } else {
-    softmax_role<C>(&tmO, p, smem, bars, w, tmem);
+    mma_pv_role<C>(p, smem, bars, w, tmem, lane);
   }
 
   ptx::tc_fence_before();

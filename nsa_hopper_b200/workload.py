@@ -60,9 +60,9 @@ def make_indices(w: Workload, seed: int = 0, B: Optional[int] = None) -> np.ndar
     return indices.generate(w.rule, B=B, Hkv=w.Hkv, T=w.T, n=w.n, block=w.block, seed=seed)
 
 
-def gathered_blocks(sel: np.ndarray, T: int, block: int, cu_seqlens: Optional[np.ndarray] = None) -> np.ndarray:
-    """Distinct selected blocks holding at least one visible key, per (b*Hkv+kvh, t): int32 [B*Hkv, T].
-    Per-token selection (BQ == 1) only."""
+def _distinct_visible(sel: np.ndarray, T: int, block: int, cu_seqlens: Optional[np.ndarray]):
+    """Per (b*Hkv+kvh, t, entry): is the entry the first occurrence of a block that holds a
+    visible key, and how many keys of it are visible.  Per-token selection (BQ == 1)."""
     B, Hkv, NQB, KSEL = sel.shape
     assert NQB == T
     s = sel.reshape(B * Hkv, T, KSEL).astype(np.int64)
@@ -77,22 +77,39 @@ def gathered_blocks(sel: np.ndarray, T: int, block: int, cu_seqlens: Optional[np
     nblk = (end - seq0 + block - 1) // block
     start = seq0[None, :, None] + s * block
     valid = (s >= 0) & (s < nblk[None, :, None]) & (start <= t[None, :, None]) & (start < end[None, :, None])
-    # first occurrence only (set semantics)
-    srt = np.sort(np.where(valid, s, -1), axis=-1)
-    distinct = (srt >= 0) & np.concatenate([np.ones_like(srt[..., :1], dtype=bool), srt[..., 1:] != srt[..., :-1]], -1)
-    return distinct.sum(-1).astype(np.int32)
+    key = np.where(valid, s, -1)
+    order = np.argsort(key, axis=-1, kind="stable")
+    srt = np.take_along_axis(key, order, -1)
+    first_sorted = (srt >= 0) & np.concatenate([np.ones_like(srt[..., :1], dtype=bool), srt[..., 1:] != srt[..., :-1]], -1)
+    first = np.zeros_like(first_sorted)
+    np.put_along_axis(first, order, first_sorted, -1)
+    last_key = np.minimum(t[None, :, None], end[None, :, None] - 1)
+    nvis = np.clip(last_key - start + 1, 0, block)
+    return first, np.where(first, nvis, 0)
 
 
-def algorithmic_work(w: Workload, sel: np.ndarray, visible_keys: np.ndarray, T: Optional[int] = None,
+def gathered_blocks(sel: np.ndarray, T: int, block: int, cu_seqlens: Optional[np.ndarray] = None) -> np.ndarray:
+    """Distinct selected blocks holding at least one visible key, per (b*Hkv+kvh, t): int32 [B*Hkv, T]."""
+    first, _ = _distinct_visible(sel, T, block, cu_seqlens)
+    return first.sum(-1).astype(np.int32)
+
+
+def visible_keys(sel: np.ndarray, T: int, block: int, cu_seqlens: Optional[np.ndarray] = None) -> np.ndarray:
+    """Keys each query token attends to, per (b*Hkv+kvh, t): int32 [B*Hkv, T]."""
+    _, nvis = _distinct_visible(sel, T, block, cu_seqlens)
+    return nvis.sum(-1).astype(np.int32)
+
+
+def algorithmic_work(w: Workload, sel: np.ndarray, T: Optional[int] = None,
                      cu_seqlens: Optional[np.ndarray] = None) -> Dict[str, float]:
-    """FLOPs and bytes of one full forward over `sel` ([B,Hkv,T,KSEL], per-token selection).
-    `visible_keys` is int [B*Hkv, T] (oracle.count_keys)."""
+    """FLOPs and bytes of one full forward over `sel` ([B,Hkv,T,KSEL], per-token selection)."""
     T = w.T if T is None else T
     B = sel.shape[0]
     G = w.G
-    keys = visible_keys.astype(np.float64).sum()
+    first, nvis = _distinct_visible(sel, T, w.block, cu_seqlens)
+    keys = nvis.astype(np.float64).sum()
     flops = G * 2.0 * (w.d_qk + w.d_v) * keys
-    nblk = gathered_blocks(sel, T, w.block, cu_seqlens).astype(np.float64).sum()
+    nblk = first.astype(np.float64).sum()
     kv_bytes = nblk * w.block * (w.d_qk + w.d_v) * 2.0
     rows = B * w.Hkv * T
     q_bytes = rows * G * w.d_qk * 2.0
