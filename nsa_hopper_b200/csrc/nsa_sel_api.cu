@@ -294,10 +294,12 @@ int launch(const nsa_sel_desc* d, nsa_stream_t stream) {
     if (rc != NSA_OK) return rc;
   }
   {
-    cuuint64_t dims[3] = {dv, (cuuint64_t)T, (cuuint64_t)B * Hkv};
-    cuuint64_t str[2] = {dv * 2, dv * 2 * T};
-    cuuint32_t box[3] = {64, 64, 1};
-    rc = encode(&tmV, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, d->v, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B,
+    // V viewed as (64 d, T, d_v/64 slices, B*Hkv): one box = a 64-key sub-block, slice-major in
+    // shared memory ([slice][row][64]), the MN-major layout the PV UMMA reads.
+    cuuint64_t dims[4] = {64, (cuuint64_t)T, dv / 64, (cuuint64_t)B * Hkv};
+    cuuint64_t str[3] = {dv * 2, 128, dv * 2 * T};
+    cuuint32_t box[4] = {64, 64, (cuuint32_t)(dv / 64), 1};
+    rc = encode(&tmV, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, d->v, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B,
                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "V");
     if (rc != NSA_OK) return rc;
   }

@@ -229,7 +229,20 @@ __device__ __forceinline__ int* info_slot(const Params& p, uint8_t* smem, int sl
 //   * sub-blocks that start after the last query token of the unit, or at/after the end of
 //     the sequence, are dropped (every key in them is masked, nsa_v0.cu:73).
 // ------------------------------------------------------------------------------------------
-__device__ int build_unit_info(const Params& p, int u, int* inf, int lane) {
+// Selection-row entry `lane` of unit u (-1 past KSEL).  The loader issues this load two units
+// ahead so its latency overlaps the K-tile traffic of the current unit.
+__device__ __forceinline__ const int32_t* unit_row(const Params& p, int u) {
+  const int per_bkv = (p.qb_end - p.qb_begin) * p.parts;
+  const int bkv_off = u / per_bkv;
+  const int qb = p.qb_begin + (u - bkv_off * per_bkv) / p.parts;
+  return p.sel + ((size_t)(p.bkv_begin + bkv_off) * p.NQB + qb) * p.KSEL;
+}
+__device__ __forceinline__ int fetch_row_entry(const Params& p, int u, int lane) {
+  return (u < p.n_units && lane < p.KSEL) ? __ldg(unit_row(p, u) + lane) : -1;
+}
+
+// `idx0` is entry `lane` of the unit's selection row (fetch_row_entry).
+__device__ int build_unit_info(const Params& p, int u, int* inf, int lane, int idx0) {
   const int per_bkv = (p.qb_end - p.qb_begin) * p.parts;
   const int bkv_off = u / per_bkv;
   const int bkv = p.bkv_begin + bkv_off;
@@ -258,7 +271,7 @@ __device__ int build_unit_info(const Params& p, int u, int* inf, int lane) {
   if (ntok > 0) {
     for (int base = 0; base < p.KSEL; base += 32) {
       const int j = base + lane;
-      const int idx = (j < p.KSEL) ? __ldg(row + j) : -1;
+      const int idx = base == 0 ? idx0 : ((j < p.KSEL) ? __ldg(row + j) : -1);
       bool valid = idx >= 0 && idx < nblk && (seq0 + idx * p.LP) <= lim;
       // set semantics: drop repeats of an earlier entry (same 32-entry group by shuffle)
 #pragma unroll 8
@@ -316,9 +329,9 @@ __device__ void loader_role(const CUtensorMap* tmQ, const CUtensorMap* tmK, cons
   uint32_t qc = 0, kc = 0;  // Q and K tile loads issued
   bool ok = true;
 
-  // Publish the info of the unit with sequence number `ui` (unit id u) and, if it has work,
-  // issue its Q tile.  Whole warp; returns false on abort.
-  auto stage_unit = [&](uint32_t ui, int u) -> bool {
+  // Publish the info of the unit with sequence number `ui` (unit id u, selection-row entry
+  // `idx` of this lane) and, if it has work, issue its Q tile.  Whole warp; false on abort.
+  auto stage_unit = [&](uint32_t ui, int u, int idx) -> bool {
     const int slot = ui % kInfoSlots;
     if (ui >= (uint32_t)kInfoSlots) {
       int r = 1;
@@ -326,7 +339,7 @@ __device__ void loader_role(const CUtensorMap* tmQ, const CUtensorMap* tmK, cons
       if (!__shfl_sync(0xffffffffu, r, 0)) return false;
     }
     int* inf = info_slot(p, smem, slot);
-    const int nsub = build_unit_info(p, u, inf, lane);
+    const int nsub = build_unit_info(p, u, inf, lane, idx);
     __syncwarp();
     if (lane == 0) ptx::mbar_arrive(&bars->info_full[slot]);
     if (nsub == 0) return true;
@@ -350,33 +363,40 @@ __device__ void loader_role(const CUtensorMap* tmQ, const CUtensorMap* tmK, cons
 
   uint32_t ui = 0;
   int u = blockIdx.x;
-  if (u < p.n_units) ok = stage_unit(0, u);
+  if (u < p.n_units) ok = stage_unit(0, u, fetch_row_entry(p, u, lane));
+  int idx_next = fetch_row_entry(p, u + gridDim.x, lane);  // row of the next unit, in flight
   for (; u < p.n_units && ok; u += gridDim.x, ++ui) {
-    // look ahead: the next unit's info and Q tile
-    if (u + (int)gridDim.x < p.n_units && !stage_unit(ui + 1, u + gridDim.x)) break;
+    // look ahead: the next unit's info and Q tile; then start fetching the row after it
+    if (u + (int)gridDim.x < p.n_units && !stage_unit(ui + 1, u + gridDim.x, idx_next)) break;
+    idx_next = fetch_row_entry(p, u + 2 * (int)gridDim.x, lane);
     const int* inf = info_slot(p, smem, ui % kInfoSlots);
     const int nsub = inf[kInfNsub];
     int r = 1;
-    if (lane == 0 && nsub > 0) {
+    if (nsub > 0) {
+      // A K tile is nsc x (DQK/64) boxes of 64 rows x 128 B; box b is issued by lane b, since the
+      // TMA throughput of one issuing thread is well below what the SM can absorb.
       const int bkv = inf[kInfBkv];
       const int nch = (nsub + 1) >> 1;
-      for (int c = 0; c < nch && r; ++c) {
+      constexpr int kNdc = C::DQK / 64;
+      for (int c = 0; c < nch; ++c) {
         const int nsc = min(2, nsub - 2 * c);
         const int ks = (int)(kc % (uint32_t)p.KS);
-        if (kc >= (uint32_t)p.KS && !w.wait(&bars->k_empty[ks], ((kc / p.KS) - 1) & 1)) { r = 0; break; }
-        uint8_t* kdst = smem + p.off_k + ks * C::kKStage;
-        ptx::mbar_arrive_expect_tx(&bars->k_full[ks], (uint32_t)(nsc * kSub * C::DQK * 2));
-        for (int j = 0; j < nsc; ++j) {
+        int go = 1;
+        if (lane == 0) {
+          go = (kc < (uint32_t)p.KS || w.wait(&bars->k_empty[ks], ((kc / p.KS) - 1) & 1)) ? 1 : 0;
+          if (go) ptx::mbar_arrive_expect_tx(&bars->k_full[ks], (uint32_t)(nsc * kSub * C::DQK * 2));
+        }
+        if (!__shfl_sync(0xffffffffu, go, 0)) { r = 0; break; }
+        if (lane < nsc * kNdc) {
+          const int j = lane / kNdc, cc = lane - j * kNdc;
           const int row = inf[kInfoHdr + 2 * c + j];
-          for (int cc = 0; cc < C::DQK / 64; ++cc)
-            ptx::tma_load_3d(kdst + cc * C::kKChunkStride + j * C::kBox, tmK, &bars->k_full[ks], cc * 64, row, bkv,
-                             pol_kv);
+          ptx::tma_load_3d(smem + p.off_k + ks * C::kKStage + cc * C::kKChunkStride + j * C::kBox, tmK,
+                           &bars->k_full[ks], cc * 64, row, bkv, pol_kv);
         }
         ++kc;
       }
     }
-    ok = __shfl_sync(0xffffffffu, r, 0) != 0;
-    kc = __shfl_sync(0xffffffffu, kc, 0);
+    ok = r != 0;
   }
   // Drain: wait until the most recent load issued into every ring stage has landed, so no
   // TMA write can reach this CTA's shared memory after it exits.
@@ -390,38 +410,44 @@ __device__ void loader_role(const CUtensorMap* tmQ, const CUtensorMap* tmK, cons
 }
 
 // ------------------------------------------------------------------------------------------
-// V loader warp (lane 0): V chunk tiles into their ring, in the same chunk order.
+// V loader warp: V chunk tiles into their ring, in the same chunk order.  Each 64-key
+// sub-block of V is one box (64 rows x DV/64 slices of 128 B) issued by its own lane.
 // ------------------------------------------------------------------------------------------
 template <class C>
 __device__ void vloader_role(const CUtensorMap* tmV, const Params& p, uint8_t* smem, SmemBars* bars,
                              const Waiter& w, int lane) {
-  if (lane == 0) {
-    const uint64_t pol_kv = ptx::policy_evict_last();
-    uint32_t ui = 0, vc = 0;
-    bool ok = true;
-    for (int u = blockIdx.x; u < p.n_units && ok; u += gridDim.x, ++ui) {
-      const int slot = ui % kInfoSlots;
-      if (!w.wait(&bars->info_full[slot], (ui / kInfoSlots) & 1)) break;
-      const int* inf = info_slot(p, smem, slot);
-      const int nsub = min(inf[kInfNsub], p.maxsub);
-      const int bkv = inf[kInfBkv];
-      const int nch = (nsub + 1) >> 1;
-      for (int c = 0; c < nch; ++c) {
-        const int nsc = min(2, nsub - 2 * c);
-        const int vs = (int)(vc % (uint32_t)p.VS);
-        if (vc >= (uint32_t)p.VS && !w.wait(&bars->v_empty[vs], ((vc / p.VS) - 1) & 1)) { ok = false; break; }
-        uint8_t* vdst = smem + p.off_v + vs * C::kVStage;
-        ptx::mbar_arrive_expect_tx(&bars->v_full[vs], (uint32_t)(nsc * kSub * C::DV * 2));
-        for (int j = 0; j < nsc; ++j) {
-          const int row = inf[kInfoHdr + 2 * c + j];
-          for (int cc = 0; cc < C::DV / 64; ++cc)
-            ptx::tma_load_3d(vdst + j * C::kVSub + cc * C::kBox, tmV, &bars->v_full[vs], cc * 64, row, bkv, pol_kv);
-        }
-        ++vc;
+  const uint64_t pol_kv = ptx::policy_evict_last();
+  uint32_t ui = 0, vc = 0;
+  bool ok = true;
+  for (int u = blockIdx.x; u < p.n_units && ok; u += gridDim.x, ++ui) {
+    const int slot = ui % kInfoSlots;
+    int got = 1;
+    if (lane == 0) got = w.wait(&bars->info_full[slot], (ui / kInfoSlots) & 1) ? 1 : 0;
+    if (!__shfl_sync(0xffffffffu, got, 0)) break;
+    const int* inf = info_slot(p, smem, slot);
+    const int nsub = min(inf[kInfNsub], p.maxsub);
+    const int bkv = inf[kInfBkv];
+    const int nch = (nsub + 1) >> 1;
+    for (int c = 0; c < nch; ++c) {
+      const int nsc = min(2, nsub - 2 * c);
+      const int vs = (int)(vc % (uint32_t)p.VS);
+      int go = 1;
+      if (lane == 0) {
+        go = (vc < (uint32_t)p.VS || w.wait(&bars->v_empty[vs], ((vc / p.VS) - 1) & 1)) ? 1 : 0;
+        if (go) ptx::mbar_arrive_expect_tx(&bars->v_full[vs], (uint32_t)(nsc * kSub * C::DV * 2));
       }
-      if (ok) ptx::mbar_arrive(&bars->info_empty[slot]);
+      if (!__shfl_sync(0xffffffffu, go, 0)) { ok = false; break; }
+      if (lane < nsc) {
+        const int row = inf[kInfoHdr + 2 * c + lane];
+        ptx::tma_load_4d(smem + p.off_v + vs * C::kVStage + lane * C::kVSub, tmV, &bars->v_full[vs], 0, row, 0, bkv,
+                         pol_kv);
+      }
+      ++vc;
     }
-    // Drain: the most recent load of every stage has landed.
+    if (ok && lane == 0) ptx::mbar_arrive(&bars->info_empty[slot]);
+  }
+  // Drain: the most recent load of every stage has landed.
+  if (lane == 0) {
     for (uint32_t s = 0; s < (uint32_t)p.VS; ++s)
       if (vc > s) w.wait_drain(&bars->v_full[s], ((s + ((vc - 1 - s) / p.VS) * p.VS) / p.VS) & 1);
   }
