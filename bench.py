@@ -21,6 +21,7 @@ import argparse
 import datetime
 import json
 import os
+import re
 import statistics
 import subprocess
 import sys
@@ -53,12 +54,14 @@ def measured_peaks():
 
 
 def committed_traffic(workload: str):
-    """DRAM bytes per launch from a committed ncu summary (profiles/), or None."""
-    path = os.path.join(REPO, "profiles", f"nsa_sel_fwd_{workload}.traffic.json")
+    """DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum of one ncu capture),
+    read from the committed summary profiles/nsa_sel_fwd_<workload>_dram.md, or None."""
+    path = os.path.join(REPO, "profiles", f"nsa_sel_fwd_{workload}_dram.md")
     try:
         with open(path) as f:
-            return float(json.load(f)["dram_bytes_per_launch"])
-    except Exception:
+            m = re.search(r"dram_bytes_per_launch\s*=\s*([0-9.eE+]+)", f.read())
+        return float(m.group(1)) if m else None
+    except OSError:
         return None
 
 

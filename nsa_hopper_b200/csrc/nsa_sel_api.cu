@@ -125,7 +125,8 @@ Variant make_variant() {
       make_variant<DQK, DV, 32, float, 1>(), make_variant<DQK, DV, 64, float, 1>()
 
 const Variant* variants(int* n) {
-  static const Variant v[] = {NSA_VARIANTS_FOR(64, 64), NSA_VARIANTS_FOR(128, 128), NSA_VARIANTS_FOR(192, 128)};
+  static const Variant v[] = {NSA_VARIANTS_FOR(64, 64), NSA_VARIANTS_FOR(128, 128), NSA_VARIANTS_FOR(192, 128),
+                              NSA_VARIANTS_FOR(128, 64)};
   *n = (int)(sizeof(v) / sizeof(v[0]));
   return v;
 }
@@ -192,7 +193,7 @@ int make_plan(const nsa_sel_desc* d, int sm_count, Plan* pl) {
   while (ncol < rows) ncol <<= 1;
   const int vi = find_variant(d->d_qk, d->d_v, ncol, d->o_dtype == NSA_DTYPE_F32 ? 1 : 0);
   if (vi < 0)
-    return fail(NSA_ERR_UNSUPPORTED, "no kernel for (d_qk=%d, d_v=%d); built: (64,64), (128,128), (192,128)",
+    return fail(NSA_ERR_UNSUPPORTED, "no kernel for (d_qk=%d, d_v=%d); built: (64,64), (128,128), (192,128), (128,64)",
                 d->d_qk, d->d_v);
   int nv = 0;
   const Variant& V = variants(&nv)[vi];

@@ -12,17 +12,18 @@
 //    KV-head-major order, so all SMs sweep the tokens of one KV head together and the
 //    gathered K/V blocks of that head are re-read from L2 rather than HBM.  K/V loads carry
 //    an L2 evict_last hint, the streaming Q loads evict_first.
-//  * Loader warp: turns a unit's selection row into a list of 64-key sub-blocks (dedupe,
+//  * K-loader warp: turns a unit's selection row into a list of 64-key sub-blocks (dedupe,
 //    padding, causal and range clipping) in a shared-memory "info" ring and issues TMA tensor
-//    loads: the unit's Q tile and, per chunk of two sub-blocks (128 keys), a K tile and a V
-//    tile into two mbarrier-driven rings.
-//  * MMA warp: one thread issues tcgen05 UMMAs in swap-AB form, so the 128 keys of a chunk
-//    are the M=128 dimension and the G*BQ query rows of the unit are N (16..64):
+//    loads: the unit's Q tile (one unit ahead) and, per chunk of two sub-blocks (128 keys),
+//    the K boxes, issued from several lanes.  A V-loader warp fills the V ring the same way
+//    (one 16 KB box per sub-block).
+//  * Two MMA warps, one issuing thread each, use tcgen05 UMMAs in swap-AB form, so the 128
+//    keys of a chunk are the M=128 dimension and the G*BQ query rows of the unit are N (16..64):
 //        S^T[keys x rows]  = K_chunk[keys x d_qk] . Q^T          (A K-major, B K-major)
 //        O^T[d_v x rows]  += V_chunk^T[d_v x keys] . P^T          (A MN-major, B K-major)
-//    It polls its barriers and issues a score MMA as soon as a K tile and one of four TMEM
-//    score buffers are free (running ahead of the softmax) and a PV MMA as soon as its P tile
-//    is ready.
+//    The score warp issues as soon as a K tile and one of four TMEM score buffers are free
+//    (running ahead of the softmax); the PV warp issues as soon as a P tile and its V tile
+//    are ready.
 //  * NWG softmax warpgroups (1 or 2): chunk g of the stream belongs to group g % NWG, which
 //    keeps its own online-softmax state and its own O^T accumulator in TMEM (a split over the
 //    unit's keys, merged by the epilogue).  Per chunk a group reads S^T from TMEM, transposes

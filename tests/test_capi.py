@@ -1,0 +1,89 @@
+"""The C ABI without a GPU: the library loads, exports every function include/nsa_sel.h declares,
+and its host-side validation and launch planning behave (nothing here launches a kernel)."""
+import ctypes
+import subprocess
+
+import pytest
+
+from nsa_hopper_b200 import capi
+
+
+def _desc(**kw):
+    base = dict(q=256, k=256, v=256, sel=256, o=256, batch=1, heads_q=64, heads_kv=4, seq_len=65536, d_qk=128,
+                d_v=128, n_qblocks=65536, n_sel=16, block_size=64, q_block=1)
+    base.update(kw)
+    return capi.make_desc(**base)
+
+
+def test_library_exports_every_header_function():
+    lib = capi.load()
+    names = capi.header_functions()
+    assert set(names) >= {"nsa_sel_forward", "nsa_sel_forward_lse", "nsa_sel_run", "nsa_sel_plan",
+                          "nsa_sel_last_error", "nsa_sel_version"}
+    for n in names:
+        assert hasattr(lib, n), n
+    assert lib.nsa_sel_version() == 10000
+
+
+def test_struct_layout_matches_header(tmp_path):
+    """The ctypes mirrors have the size and field offsets the C compiler gives the header's structs."""
+    fields = [f for f, _ in capi.NsaSelDesc._fields_]
+    pfields = [f for f, _ in capi.NsaSelPlanInfo._fields_]
+    src = tmp_path / "layout.c"
+    lines = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{capi.HEADER_PATH}"', "int main(void) {",
+             'printf("%zu\\n", sizeof(nsa_sel_desc));', 'printf("%zu\\n", sizeof(nsa_sel_plan_info));']
+    lines += [f'printf("%zu\\n", offsetof(nsa_sel_desc, {f}));' for f in fields]
+    lines += [f'printf("%zu\\n", offsetof(nsa_sel_plan_info, {f}));' for f in pfields]
+    lines += ["return 0; }"]
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-o", str(exe), str(src)], check=True)
+    vals = [int(x) for x in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split()]
+    assert vals[0] == ctypes.sizeof(capi.NsaSelDesc) and vals[1] == ctypes.sizeof(capi.NsaSelPlanInfo)
+    got = vals[2:]
+    want = [getattr(capi.NsaSelDesc, f).offset for f in fields] + [getattr(capi.NsaSelPlanInfo, f).offset for f in pfields]
+    assert got == want
+
+
+def test_plan_north_star():
+    p = capi.plan(_desc())
+    assert p["n_cols"] == 16 and p["q_per_unit"] == 1 and p["parts"] == 1
+    assert p["n_units"] == 4 * 65536 and p["grid"] == 148
+    assert p["smem_bytes"] <= 232448 and p["k_stages"] >= 2 and p["v_stages"] >= 2
+
+
+def test_plan_query_block_mode_splits_wide_groups():
+    # G = 16 with BQ = 16 would be 256 columns: split into parts of 4 tokens (N = 64)
+    p = capi.plan(_desc(heads_q=16, heads_kv=1, seq_len=768, n_qblocks=48, n_sel=6, d_qk=64, d_v=64, q_block=16,
+                        o_dtype=capi.DTYPE_F32))
+    assert p["n_cols"] == 64 and p["q_per_unit"] == 4 and p["parts"] == 4 and p["n_units"] == 48 * 4
+
+
+def test_plan_small_group_pads_columns():
+    p = capi.plan(_desc(heads_q=32, heads_kv=8))  # G = 4 -> one N=16 tile per token
+    assert p["n_cols"] == 16
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(q=0), capi.NSA_ERR_INVALID_ARG),
+    (dict(q=258), capi.NSA_ERR_INVALID_ARG),               # TMA needs 16-byte aligned bases
+    (dict(heads_q=63), capi.NSA_ERR_INVALID_ARG),          # Hq % Hkv != 0
+    (dict(n_qblocks=100), capi.NSA_ERR_INVALID_ARG),       # NQB != ceil(T/BQ)
+    (dict(block_size=96), capi.NSA_ERR_UNSUPPORTED),
+    (dict(d_qk=96), capi.NSA_ERR_UNSUPPORTED),
+    (dict(o_dtype=7), capi.NSA_ERR_INVALID_ARG),
+    (dict(cu_seqlens=256, batch=2, n_qblocks=65536), capi.NSA_ERR_INVALID_ARG),
+    (dict(bkv_begin=3, bkv_end=2), capi.NSA_ERR_INVALID_ARG),
+    (dict(qb_begin=70000), capi.NSA_ERR_INVALID_ARG),
+    (dict(n_sel=200), capi.NSA_ERR_UNSUPPORTED),           # more than 128 sub-blocks per unit
+])
+def test_validation_errors(kw, code):
+    with pytest.raises(capi.NsaSelError) as e:
+        capi.plan(_desc(**kw))
+    assert e.value.code == code
+    assert capi.last_error() != ""
+
+
+def test_shard_plan_counts_units():
+    p = capi.plan(_desc(bkv_begin=1, bkv_end=3, qb_begin=100, qb_end=1100))
+    assert p["n_units"] == 2 * 1000
