@@ -148,6 +148,42 @@ def shard_for(args, w, rank, world):
     return args.seed, plans[rank]
 
 
+def time_gather(o, lse, sh, w, world, stream, reps: int = 3):
+    """Optional NCCL all-gather of each rank's O (bf16) and LSE rows over NVLink, timed on its
+    own after the forward's timed region (the forward itself needs no collective).  Each rank
+    packs its shard's rows once, untimed; shards of unequal size are padded to the largest."""
+    import torch
+    import torch.distributed as dist
+
+    if sh is None:
+        parts = [o.reshape(-1).view(torch.uint8), lse.reshape(-1).view(torch.uint8)]
+    else:
+        b0, b1, q0, q1 = sh
+        G = w.Hq // w.Hkv
+        parts = []
+        for bkv in range(b0, b1):
+            b, kvh = divmod(bkv, w.Hkv)
+            parts.append(o[b, kvh * G:(kvh + 1) * G, q0:q1].reshape(-1).view(torch.uint8))
+            parts.append(lse[b, kvh * G:(kvh + 1) * G, q0:q1].reshape(-1).view(torch.uint8))
+    n = sum(p.numel() for p in parts)
+    nmax = int(reduce_max(float(n), world))
+    send = torch.zeros(nmax, dtype=torch.uint8, device=o.device)
+    torch.cat(parts, out=send[:n])
+    recv = torch.empty(nmax * world, dtype=torch.uint8, device=o.device)
+    dist.all_gather_into_tensor(recv, send)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        dist.all_gather_into_tensor(recv, send)
+    e1.record(stream)
+    barrier(world)
+    ms = reduce_max(e0.elapsed_time(e1) / reps, world)
+    del recv, send
+    return {"ms": ms, "bytes_per_rank": nmax, "busbw_gbs": nmax * (world - 1) / (ms * 1e-3) / 1e9,
+            "what": "NCCL all_gather_into_tensor of each rank's O (bf16) + LSE rows, timed separately"}
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
 
@@ -257,6 +293,10 @@ def run_ours(args, rank, world, local_rank):
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": ksteps,
                "path": "C ABI nsa_sel_run with pinned host Q/K/V/sel in, O/LSE out"}
 
+    gather = None
+    if world > 1 and not args.no_gather:
+        gather = time_gather(o, lse, sh, w, world, stream)
+
     hbm_peak, tf_peak, peak_kind = measured_peaks()
     tokens_job = work["tokens"] * frac_units * world
     flops_rank = work["flops"] * frac_units
@@ -292,6 +332,7 @@ def run_ours(args, rank, world, local_rank):
                          "tensor_frac": flops_rank / (mean_ms * 1e-3) / (tf_peak * 1e12),
                          "kernel_ms": mean_ms},
             "e2e": e2e,
+            "gather": gather,
             "clocks": clocks,
             "gpu_launches": args.steps,
             "step_ms": step_ms,
@@ -369,6 +410,7 @@ def main():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gather", action="store_true", help="skip the separately timed all-gather (N > 1)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 

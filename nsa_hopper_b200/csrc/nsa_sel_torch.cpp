@@ -30,7 +30,7 @@ namespace {
 // units that a harness compiles with its own flags (e.g. nvcc host code in a JIT build).
 thread_local char g_msg[768];
 
-const char* fmt(const char* f, ...) {
+const char* format_msg(const char* f, ...) {
   va_list ap;
   va_start(ap, f);
   vsnprintf(g_msg, sizeof(g_msg), f, ap);
@@ -75,7 +75,7 @@ const Api& api() {
     a.version = reinterpret_cast<decltype(a.version)>(dlsym(h, "nsa_sel_version"));
   });
   if (!(a.forward && a.run && a.last_error && a.version))
-    TORCH_CHECK(false, fmt("libnsa_sel.so could not be loaded (build it first): %s", error.c_str()));
+    TORCH_CHECK(false, format_msg("libnsa_sel.so could not be loaded (build it first): %s", error.c_str()));
   return a;
 }
 
@@ -99,7 +99,7 @@ void check_inputs(const torch::Tensor& Q, const torch::Tensor& K, const torch::T
 }
 
 int32_t i32(int64_t x, const char* what) {
-  if (!(x >= 0 && x < (int64_t(1) << 31))) TORCH_CHECK(false, fmt("%s out of int32 range", what));
+  if (!(x >= 0 && x < (int64_t(1) << 31))) TORCH_CHECK(false, format_msg("%s out of int32 range", what));
   return static_cast<int32_t>(x);
 }
 
@@ -121,7 +121,7 @@ torch::Tensor forward(torch::Tensor Q, torch::Tensor K, torch::Tensor V, torch::
                            i32(Q.size(2), "S"), i32(Q.size(3), "D"), i32(sel.size(2), "NQB"),
                            i32(sel.size(3), "KSEL"), i32(l_prime, "l_prime"), i32(BQ, "BQ"),
                            reinterpret_cast<nsa_stream_t>(c10::cuda::getCurrentCUDAStream().stream()));
-  if (rc != NSA_OK) TORCH_CHECK(false, fmt("nsa_sel_forward failed (%d): %s", rc, a.last_error()));
+  if (rc != NSA_OK) TORCH_CHECK(false, format_msg("nsa_sel_forward failed (%d): %s", rc, a.last_error()));
   return O;
 }
 
@@ -162,7 +162,7 @@ std::vector<torch::Tensor> forward_lse(torch::Tensor Q, torch::Tensor K, torch::
   d.o_dtype = out_f32 ? NSA_DTYPE_F32 : NSA_DTYPE_BF16;
   d.scale = static_cast<float>(scale);
   const int rc = a.run(&d, reinterpret_cast<nsa_stream_t>(c10::cuda::getCurrentCUDAStream().stream()));
-  if (rc != NSA_OK) TORCH_CHECK(false, fmt("nsa_sel_run failed (%d): %s", rc, a.last_error()));
+  if (rc != NSA_OK) TORCH_CHECK(false, format_msg("nsa_sel_run failed (%d): %s", rc, a.last_error()));
   return {O, L};
 }
 

@@ -47,3 +47,37 @@ def test_reference_harness_flow(mod, B, Hq, Hkv, S, D, KSEL, BQ):
     w, mm = cyc[0::2].float().mean().item(), cyc[1::2].float().mean().item()
     assert w + mm > 0 and 0.0 <= w / (w + mm) <= 1.0
 
+
+
+def test_reference_harness_error_path_raises(mod):
+    """An unsupported shape raises RuntimeError through the JIT-built module, as the reference's
+    TORCH_CHECK does (nsa_v2.cu:151-152,166).  Run in a child process so that a host-side crash
+    shows up as a failed test instead of ending the test session."""
+    import subprocess
+    import sys
+    import textwrap
+
+    code = textwrap.dedent(f"""
+        import torch
+        from torch.utils.cpp_extension import load
+        mod = load("nsa_v2", [{SRC!r}], extra_cuda_cflags=["-arch=sm_90a", "-O3", "--use_fast_math",
+                   "--expt-relaxed-constexpr"], extra_include_paths=["/workspace/nsa/cutlass/include"], verbose=False)
+        q = torch.randn(1, 4, 128, 96, device="cuda", dtype=torch.bfloat16)   # D = 96: unsupported
+        k = torch.randn(1, 2, 128, 96, device="cuda", dtype=torch.bfloat16)
+        sel = torch.zeros(1, 2, 8, 2, dtype=torch.int32, device="cuda")
+        cyc = torch.empty(0, dtype=torch.int64, device="cuda")
+        for call in (lambda: mod.forward(q, k, k, sel, 64, 16, cyc),
+                     lambda: mod.forward_lse(q, k, k, sel, 64, 16, None, 0.0, False)):
+            try:
+                call()
+                print("no error")
+            except RuntimeError as e:
+                print("raised:", str(e).splitlines()[0][:160])
+        torch.cuda.synchronize()
+        print("context ok")
+    """)
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = r.stdout.splitlines()
+    assert sum(l.startswith("raised:") and "failed" in l for l in lines) == 2, r.stdout
+    assert "context ok" in lines
