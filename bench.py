@@ -428,6 +428,9 @@ def main():
         import torch
         import torch.distributed as dist
 
+        # NCCL_DEBUG=VERSION prints a banner on stdout, where rank 0's JSON line must stand alone.
+        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
+            os.environ["NCCL_DEBUG"] = "WARN"
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))

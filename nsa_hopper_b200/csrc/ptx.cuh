@@ -92,7 +92,7 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
   return p;
 }
 
-// ---------------------------------------------------------------- TMA (no multicast anywhere)
+// ---------------------------------------------------------------- TMA (plain, CTA-local destination)
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
                                             int c2, uint64_t policy) {
   asm volatile(
