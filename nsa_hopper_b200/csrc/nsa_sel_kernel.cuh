@@ -52,11 +52,11 @@ constexpr int kInfoHdr = 16;      // ints of header per info slot
 constexpr int kMaxStages = 8;     // upper bound on K and V ring depth
 constexpr int kSSlots = 4;        // TMEM score buffers (MMA look-ahead)
 constexpr int kQSlots = 3;        // Q tile ring (the loader stages one unit ahead)
-constexpr int kLoaderWarp = 0;    // unit info, Q tiles and K tiles
+constexpr int kLoaderWarp = 0;    // K tiles
 constexpr int kMmaWarp = 1;       // score MMAs; owns the TMEM allocation
 constexpr int kEpiWarp0 = 2;      // warps 2..5: epilogue
-constexpr int kSoftWarp0 = 6;     // warps 6..6+4*NWG-1: softmax warpgroups; then the V loader and
-                                  // the PV MMA warp
+constexpr int kSoftWarp0 = 6;     // warps 6..6+4*NWG-1: softmax warpgroups; then the V loader, the
+                                  // PV MMA warp and the scheduler (unit info and Q tiles)
 constexpr uint32_t kEpiBar = 1;   // named barrier of the epilogue warpgroup
 constexpr uint32_t kWgBar0 = 2;   // named barrier of softmax warpgroup w = kWgBar0 + w
 constexpr float kRescaleLog2 = 8.0f;
@@ -64,7 +64,22 @@ constexpr int kDevErrTimeout = 1;
 
 __host__ __device__ constexpr int vloader_warp(int nwg) { return kSoftWarp0 + 4 * nwg; }
 __host__ __device__ constexpr int pv_warp(int nwg) { return kSoftWarp0 + 4 * nwg + 1; }
-__host__ __device__ constexpr int threads_for(int nwg) { return 32 * (pv_warp(nwg) + 1); }
+__host__ __device__ constexpr int sched_warp(int nwg) { return kSoftWarp0 + 4 * nwg + 2; }
+__host__ __device__ constexpr int threads_for(int nwg) { return 32 * (sched_warp(nwg) + 1); }
+
+// Position in a ring of `n` slots: slot index and the parity of the lap (the mbarrier phase of
+// a "full" wait; an "empty" wait of a later lap uses the opposite parity).
+struct Ring {
+  uint32_t idx = 0, phase = 0;
+  bool lapped = false;  // true once every slot has been used at least once
+  __device__ __forceinline__ void next(uint32_t n) {
+    if (++idx == n) {
+      idx = 0;
+      phase ^= 1u;
+      lapped = true;
+    }
+  }
+};
 
 // Info-slot header fields.
 enum : int { kInfNsub = 0, kInfT0, kInfNtok, kInfKend, kInfB, kInfKvh, kInfBkv, kInfSeq0, kInfRef };
@@ -274,12 +289,8 @@ __device__ int build_unit_info(const Params& p, int u, int* inf, int lane, int i
       const int j = base + lane;
       const int idx = base == 0 ? idx0 : ((j < p.KSEL) ? __ldg(row + j) : -1);
       bool valid = idx >= 0 && idx < nblk && (seq0 + idx * p.LP) <= lim;
-      // set semantics: drop repeats of an earlier entry (same 32-entry group by shuffle)
-#pragma unroll 8
-      for (int k2 = 0; k2 < 32; ++k2) {
-        const int other = __shfl_sync(0xffffffffu, idx, k2);
-        if (k2 < lane && other == idx) valid = false;
-      }
+      // set semantics: drop repeats of an earlier entry (same 32-entry group)
+      if ((__match_any_sync(0xffffffffu, idx) & ((1u << lane) - 1u)) != 0u) valid = false;
       if (valid && base > 0) {  // earlier groups (KSEL > 32 only)
         for (int k2 = 0; k2 < base; ++k2)
           if (__ldg(row + k2) == idx) { valid = false; break; }
@@ -317,95 +328,109 @@ __device__ int build_unit_info(const Params& p, int u, int* inf, int lane, int i
 }
 
 // ------------------------------------------------------------------------------------------
-// Loader warp: info ring + TMA loads of Q and K tiles.  It runs one unit ahead for the unit
-// info and the Q tile (a three-deep Q ring), so the next unit's Q is already resident when the
-// score MMAs reach it; the unit's K chunk tiles follow in ring order.  V tiles have their own
-// loader warp, so neither ring waits for the other's slots.
+// Scheduler warp: decodes each unit into the info ring and loads its Q tile (three-deep Q
+// ring), running ahead of the consumers; the selection row of the unit after next is already in
+// flight while a unit is decoded.
 // ------------------------------------------------------------------------------------------
 template <class C>
-__device__ void loader_role(const CUtensorMap* tmQ, const CUtensorMap* tmK, const CUtensorMap* tmV,
-                            const Params& p, uint8_t* smem, SmemBars* bars, const Waiter& w, int lane) {
-  const uint64_t pol_kv = ptx::policy_evict_last();
+__device__ void scheduler_role(const CUtensorMap* tmQ, const Params& p, uint8_t* smem, SmemBars* bars,
+                               const Waiter& w, int lane) {
   const uint64_t pol_q = ptx::policy_evict_first();
-  uint32_t qc = 0, kc = 0;  // Q and K tile loads issued
+  Ring info, q;
   bool ok = true;
-
-  // Publish the info of the unit with sequence number `ui` (unit id u, selection-row entry
-  // `idx` of this lane) and, if it has work, issue its Q tile.  Whole warp; false on abort.
-  auto stage_unit = [&](uint32_t ui, int u, int idx) -> bool {
-    const int slot = ui % kInfoSlots;
-    if (ui >= (uint32_t)kInfoSlots) {
+  int idx = fetch_row_entry(p, blockIdx.x, lane);
+  for (int u = blockIdx.x; u < p.n_units && ok; u += gridDim.x) {
+    const int idx_next = fetch_row_entry(p, u + gridDim.x, lane);  // next row, in flight
+    if (info.lapped) {
       int r = 1;
-      if (lane == 0) r = w.wait(&bars->info_empty[slot], ((ui / kInfoSlots) - 1) & 1) ? 1 : 0;
-      if (!__shfl_sync(0xffffffffu, r, 0)) return false;
+      if (lane == 0) r = w.wait(&bars->info_empty[info.idx], info.phase ^ 1u) ? 1 : 0;
+      if (!__shfl_sync(0xffffffffu, r, 0)) break;
     }
-    int* inf = info_slot(p, smem, slot);
+    int* inf = info_slot(p, smem, info.idx);
     const int nsub = build_unit_info(p, u, inf, lane, idx);
     __syncwarp();
-    if (lane == 0) ptx::mbar_arrive(&bars->info_full[slot]);
-    if (nsub == 0) return true;
+    if (lane == 0) ptx::mbar_arrive(&bars->info_full[info.idx]);
+    info.next(kInfoSlots);
+    idx = idx_next;
+    if (nsub == 0) continue;
     int r = 1;
     if (lane == 0) {
       const int t0 = inf[kInfT0], b = inf[kInfB], kvh = inf[kInfKvh];
-      const int qbuf = qc % kQSlots;
-      if (qc >= (uint32_t)kQSlots && !w.wait(&bars->q_empty[qbuf], ((qc / kQSlots) - 1) & 1)) {
+      if (q.lapped && !w.wait(&bars->q_empty[q.idx], q.phase ^ 1u)) {
         r = 0;
       } else {
-        uint8_t* qdst = smem + p.off_q + qbuf * C::kQBytes;
-        ptx::mbar_arrive_expect_tx(&bars->q_full[qbuf], (uint32_t)(C::DQK * p.BQs * p.G * 2));
+        uint8_t* qdst = smem + p.off_q + q.idx * C::kQBytes;
+        ptx::mbar_arrive_expect_tx(&bars->q_full[q.idx], (uint32_t)(C::DQK * p.BQs * p.G * 2));
         for (int cc = 0; cc < C::DQK / 64; ++cc)
-          ptx::tma_load_4d(qdst + cc * C::kQChunk, tmQ, &bars->q_full[qbuf], cc * 64, t0, kvh * p.G, b, pol_q);
-        ++qc;
+          ptx::tma_load_4d(qdst + cc * C::kQChunk, tmQ, &bars->q_full[q.idx], cc * 64, t0, kvh * p.G, b, pol_q);
       }
     }
-    qc = __shfl_sync(0xffffffffu, qc, 0);
-    return __shfl_sync(0xffffffffu, r, 0) != 0;
-  };
+    ok = __shfl_sync(0xffffffffu, r, 0) != 0;
+    if (ok) q.next(kQSlots);
+  }
+  // Drain: the most recent Q load of every slot has landed.
+  if (lane == 0) {
+    Ring d = q;
+    for (int s2 = 0; s2 < kQSlots; ++s2) {
+      // slot d.idx - 1 - s2 (mod kQSlots), lap parity adjusted when it wraps
+      const uint32_t back = (uint32_t)s2 + 1u;
+      const uint32_t slot = (d.idx + kQSlots - back % kQSlots) % kQSlots;
+      const uint32_t ph = (d.idx >= back) ? d.phase : (d.phase ^ 1u);
+      if (d.lapped || d.idx >= back) w.wait_drain(&bars->q_full[slot], ph);
+    }
+  }
+  __syncwarp();
+}
 
-  uint32_t ui = 0;
-  int u = blockIdx.x;
-  if (u < p.n_units) ok = stage_unit(0, u, fetch_row_entry(p, u, lane));
-  int idx_next = fetch_row_entry(p, u + gridDim.x, lane);  // row of the next unit, in flight
-  for (; u < p.n_units && ok; u += gridDim.x, ++ui) {
-    // look ahead: the next unit's info and Q tile; then start fetching the row after it
-    if (u + (int)gridDim.x < p.n_units && !stage_unit(ui + 1, u + gridDim.x, idx_next)) break;
-    idx_next = fetch_row_entry(p, u + 2 * (int)gridDim.x, lane);
-    const int* inf = info_slot(p, smem, ui % kInfoSlots);
-    const int nsub = inf[kInfNsub];
-    int r = 1;
-    if (nsub > 0) {
-      // A K tile is nsc x (DQK/64) boxes of 64 rows x 128 B; box b is issued by lane b, since the
-      // TMA throughput of one issuing thread is well below what the SM can absorb.
-      const int bkv = inf[kInfBkv];
-      const int nch = (nsub + 1) >> 1;
-      constexpr int kNdc = C::DQK / 64;
-      for (int c = 0; c < nch; ++c) {
-        const int nsc = min(2, nsub - 2 * c);
-        const int ks = (int)(kc % (uint32_t)p.KS);
-        int go = 1;
-        if (lane == 0) {
-          go = (kc < (uint32_t)p.KS || w.wait(&bars->k_empty[ks], ((kc / p.KS) - 1) & 1)) ? 1 : 0;
-          if (go) ptx::mbar_arrive_expect_tx(&bars->k_full[ks], (uint32_t)(nsc * kSub * C::DQK * 2));
-        }
-        if (!__shfl_sync(0xffffffffu, go, 0)) { r = 0; break; }
-        if (lane < nsc * kNdc) {
-          const int j = lane / kNdc, cc = lane - j * kNdc;
-          const int row = inf[kInfoHdr + 2 * c + j];
-          ptx::tma_load_3d(smem + p.off_k + ks * C::kKStage + cc * C::kKChunkStride + j * C::kBox, tmK,
-                           &bars->k_full[ks], cc * 64, row, bkv, pol_kv);
-        }
-        ++kc;
+// ------------------------------------------------------------------------------------------
+// K loader warp: the K chunk tiles of each unit into their ring, in chunk order.  A K tile is
+// nsc x (DQK/64) boxes of 64 rows x 128 B; box b is issued by lane b, since the TMA throughput of
+// one issuing thread is well below what the SM can absorb.  Everything but the issue itself is
+// computed before the wait for a free slot.
+// ------------------------------------------------------------------------------------------
+template <class C>
+__device__ void kloader_role(const CUtensorMap* tmK, const Params& p, uint8_t* smem, SmemBars* bars,
+                             const Waiter& w, int lane) {
+  const uint64_t pol_kv = ptx::policy_evict_last();
+  constexpr int kNdc = C::DQK / 64;
+  const int j = lane / kNdc, cc = lane - (lane / kNdc) * kNdc;  // this lane's (sub-block, d slice)
+  uint8_t* kdst0 = smem + p.off_k + cc * C::kKChunkStride + j * C::kBox;
+  Ring info, k;
+  bool ok = true;
+  for (int u = blockIdx.x; u < p.n_units && ok; u += gridDim.x) {
+    int got = 1;
+    if (lane == 0) got = w.wait(&bars->info_full[info.idx], info.phase) ? 1 : 0;
+    if (!__shfl_sync(0xffffffffu, got, 0)) break;
+    const int* inf = info_slot(p, smem, info.idx);
+    const int nsub = min(inf[kInfNsub], p.maxsub);
+    const int bkv = inf[kInfBkv];
+    const int nch = (nsub + 1) >> 1;
+    for (int c = 0; c < nch; ++c) {
+      const int nsc = min(2, nsub - 2 * c);
+      const bool mine = lane < nsc * kNdc;
+      const int row = mine ? inf[kInfoHdr + 2 * c + j] : 0;
+      uint8_t* dst = kdst0 + k.idx * C::kKStage;
+      int go = 1;
+      if (lane == 0) {
+        go = (!k.lapped || w.wait(&bars->k_empty[k.idx], k.phase ^ 1u)) ? 1 : 0;
+        if (go) ptx::mbar_arrive_expect_tx(&bars->k_full[k.idx], (uint32_t)(nsc * kSub * C::DQK * 2));
       }
+      if (!__shfl_sync(0xffffffffu, go, 0)) { ok = false; break; }
+      if (mine) ptx::tma_load_3d(dst, tmK, &bars->k_full[k.idx], cc * 64, row, bkv, pol_kv);
+      k.next((uint32_t)p.KS);
     }
-    ok = r != 0;
+    if (ok && lane == 0) ptx::mbar_arrive(&bars->info_empty[info.idx]);
+    info.next(kInfoSlots);
   }
   // Drain: wait until the most recent load issued into every ring stage has landed, so no
   // TMA write can reach this CTA's shared memory after it exits.
   if (lane == 0) {
-    for (uint32_t s = 0; s < (uint32_t)p.KS; ++s)
-      if (kc > s) w.wait_drain(&bars->k_full[s], ((s + ((kc - 1 - s) / p.KS) * p.KS) / p.KS) & 1);
-    for (uint32_t s = 0; s < (uint32_t)kQSlots; ++s)
-      if (qc > s) w.wait_drain(&bars->q_full[s], ((s + ((qc - 1 - s) / kQSlots) * kQSlots) / kQSlots) & 1);
+    for (int s2 = 0; s2 < p.KS; ++s2) {
+      const uint32_t back = (uint32_t)s2 + 1u;
+      const uint32_t slot = (k.idx + (uint32_t)p.KS - back % (uint32_t)p.KS) % (uint32_t)p.KS;
+      const uint32_t ph = (k.idx >= back) ? k.phase : (k.phase ^ 1u);
+      if (k.lapped || k.idx >= back) w.wait_drain(&bars->k_full[slot], ph);
+    }
   }
   __syncwarp();
 }
@@ -418,39 +443,42 @@ template <class C>
 __device__ void vloader_role(const CUtensorMap* tmV, const Params& p, uint8_t* smem, SmemBars* bars,
                              const Waiter& w, int lane) {
   const uint64_t pol_kv = ptx::policy_evict_last();
-  uint32_t ui = 0, vc = 0;
+  uint8_t* vdst0 = smem + p.off_v + lane * C::kVSub;
+  Ring info, v;
   bool ok = true;
-  for (int u = blockIdx.x; u < p.n_units && ok; u += gridDim.x, ++ui) {
-    const int slot = ui % kInfoSlots;
+  for (int u = blockIdx.x; u < p.n_units && ok; u += gridDim.x) {
     int got = 1;
-    if (lane == 0) got = w.wait(&bars->info_full[slot], (ui / kInfoSlots) & 1) ? 1 : 0;
+    if (lane == 0) got = w.wait(&bars->info_full[info.idx], info.phase) ? 1 : 0;
     if (!__shfl_sync(0xffffffffu, got, 0)) break;
-    const int* inf = info_slot(p, smem, slot);
+    const int* inf = info_slot(p, smem, info.idx);
     const int nsub = min(inf[kInfNsub], p.maxsub);
     const int bkv = inf[kInfBkv];
     const int nch = (nsub + 1) >> 1;
     for (int c = 0; c < nch; ++c) {
       const int nsc = min(2, nsub - 2 * c);
-      const int vs = (int)(vc % (uint32_t)p.VS);
+      const bool mine = lane < nsc;
+      const int row = mine ? inf[kInfoHdr + 2 * c + lane] : 0;
+      uint8_t* dst = vdst0 + v.idx * C::kVStage;
       int go = 1;
       if (lane == 0) {
-        go = (vc < (uint32_t)p.VS || w.wait(&bars->v_empty[vs], ((vc / p.VS) - 1) & 1)) ? 1 : 0;
-        if (go) ptx::mbar_arrive_expect_tx(&bars->v_full[vs], (uint32_t)(nsc * kSub * C::DV * 2));
+        go = (!v.lapped || w.wait(&bars->v_empty[v.idx], v.phase ^ 1u)) ? 1 : 0;
+        if (go) ptx::mbar_arrive_expect_tx(&bars->v_full[v.idx], (uint32_t)(nsc * kSub * C::DV * 2));
       }
       if (!__shfl_sync(0xffffffffu, go, 0)) { ok = false; break; }
-      if (lane < nsc) {
-        const int row = inf[kInfoHdr + 2 * c + lane];
-        ptx::tma_load_4d(smem + p.off_v + vs * C::kVStage + lane * C::kVSub, tmV, &bars->v_full[vs], 0, row, 0, bkv,
-                         pol_kv);
-      }
-      ++vc;
+      if (mine) ptx::tma_load_4d(dst, tmV, &bars->v_full[v.idx], 0, row, 0, bkv, pol_kv);
+      v.next((uint32_t)p.VS);
     }
-    if (ok && lane == 0) ptx::mbar_arrive(&bars->info_empty[slot]);
+    if (ok && lane == 0) ptx::mbar_arrive(&bars->info_empty[info.idx]);
+    info.next(kInfoSlots);
   }
   // Drain: the most recent load of every stage has landed.
   if (lane == 0) {
-    for (uint32_t s = 0; s < (uint32_t)p.VS; ++s)
-      if (vc > s) w.wait_drain(&bars->v_full[s], ((s + ((vc - 1 - s) / p.VS) * p.VS) / p.VS) & 1);
+    for (int s2 = 0; s2 < p.VS; ++s2) {
+      const uint32_t back = (uint32_t)s2 + 1u;
+      const uint32_t slot = (v.idx + (uint32_t)p.VS - back % (uint32_t)p.VS) % (uint32_t)p.VS;
+      const uint32_t ph = (v.idx >= back) ? v.phase : (v.phase ^ 1u);
+      if (v.lapped || v.idx >= back) w.wait_drain(&bars->v_full[slot], ph);
+    }
   }
   __syncwarp();
 }
@@ -472,7 +500,8 @@ __device__ void mma_s_role(const Params& p, uint8_t* smem, SmemBars* bars, const
     bool ok = true;
     // Error-path test hook: a bounded wait that can only end by running out of time.
     if (p.debug_stall) ok = w.wait(&bars->stall, 0);
-    uint32_t g = 0, kc = 0, ui = 0, ne = 0;
+    uint32_t g = 0, ui = 0, ne = 0;
+    Ring k;
     const uint32_t k_base = ptx::smem_u32(smem + p.off_k);
     const uint32_t q_base = ptx::smem_u32(smem + p.off_q);
     for (int u = blockIdx.x; u < p.n_units && ok; u += gridDim.x, ++ui) {
@@ -487,15 +516,15 @@ __device__ void mma_s_role(const Params& p, uint8_t* smem, SmemBars* bars, const
         long long t_wait = 0;
         if (!w.wait(&bars->q_full[qs], (ne / kQSlots) & 1)) break;
         const uint64_t bq0 = ptx::sdesc_sw128(q_base + qs * C::kQBytes, 16, 1024);
-        for (int c = 0; c < nch; ++c, ++g, ++kc) {
+        for (int c = 0; c < nch; ++c, ++g, k.next((uint32_t)p.KS)) {
           const int sslot = g % kSSlots;
-          const int ks = kc % p.KS;
+          const uint32_t ks = k.idx;
+          const uint64_t a0 = ptx::sdesc_sw128(k_base + ks * C::kKStage, 16, 1024);
           if (g >= (uint32_t)kSSlots && !w.wait(&bars->s_empty[sslot], ((g / kSSlots) - 1) & 1)) { ok = false; break; }
           const long long t0 = clock64();
-          if (!w.wait(&bars->k_full[ks], (kc / p.KS) & 1)) { ok = false; break; }
+          if (!w.wait(&bars->k_full[ks], k.phase)) { ok = false; break; }
           t_wait += clock64() - t0;
           ptx::tc_fence_after();
-          const uint64_t a0 = ptx::sdesc_sw128(k_base + ks * C::kKStage, 16, 1024);
           const uint32_t dS = tmem + C::kTmemS + sslot * C::NCOL;
 #pragma unroll
           for (int j = 0; j < C::DQK / 16; ++j) {
@@ -526,7 +555,8 @@ __device__ void mma_pv_role(const Params& p, uint8_t* smem, SmemBars* bars, cons
                             int lane) {
   if (lane == 0) {
     bool ok = true;
-    uint32_t vc = 0, ui = 0, ne = 0;
+    uint32_t ui = 0, ne = 0;
+    Ring v;
     uint32_t kc0 = 0, kc1 = 0;  // chunks so far of softmax group 0 / 1
     const uint32_t v_base = ptx::smem_u32(smem + p.off_v);
     const uint32_t p_base = ptx::smem_u32(smem + p.off_p);
@@ -540,22 +570,22 @@ __device__ void mma_pv_role(const Params& p, uint8_t* smem, SmemBars* bars, cons
       if (nch > 0) {
         const long long t_unit0 = clock64();
         long long t_wait = 0;
-        for (int c = 0; c < nch; ++c, ++vc) {
+        for (int c = 0; c < nch; ++c, v.next((uint32_t)p.VS)) {
           const int wg = c % C::NWG;
           const uint32_t k = wg ? kc1++ : kc0++;
           const int ps = pslot_of<C::NWG>(wg, k);
           const int nsc = min(2, nsub - 2 * c);
-          const int vs = vc % p.VS;
+          const uint32_t vs = v.idx;
           const bool first = c < C::NWG;
-          if (!w.wait(&bars->p_full[ps], pphase_of<C::NWG>(k) & 1)) { ok = false; break; }
-          if (first && ne >= 2 && !w.wait(&bars->o_empty[ne & 1], ((ne >> 1) - 1) & 1)) { ok = false; break; }
-          const long long t0 = clock64();
-          if (!w.wait(&bars->v_full[vs], (vc / p.VS) & 1)) { ok = false; break; }
-          t_wait += clock64() - t0;
-          ptx::tc_fence_after();
           const uint64_t a0 = ptx::sdesc_sw128(v_base + vs * C::kVStage, C::kBox, 1024);
           const uint64_t b0 = ptx::sdesc_sw128(p_base + ps * C::kPBytes, 16, 1024);
           const uint32_t dO = tmem + C::kTmemO + (wg * 2 + (ne & 1)) * C::NCOL;
+          if (!w.wait(&bars->p_full[ps], pphase_of<C::NWG>(k) & 1)) { ok = false; break; }
+          if (first && ne >= 2 && !w.wait(&bars->o_empty[ne & 1], ((ne >> 1) - 1) & 1)) { ok = false; break; }
+          const long long t0 = clock64();
+          if (!w.wait(&bars->v_full[vs], v.phase)) { ok = false; break; }
+          t_wait += clock64() - t0;
+          ptx::tc_fence_after();
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             if (j < nsc * 4) {
@@ -894,7 +924,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kInfoSlots; ++s) {
       ptx::mbar_init(&bars->info_full[s], 1);
-      ptx::mbar_init(&bars->info_empty[s], 4 + C::NWG);  // 2 MMA warps, V loader, epilogue, each softmax group
+      ptx::mbar_init(&bars->info_empty[s], 5 + C::NWG);  // 2 MMA warps, K and V loaders, epilogue, softmax groups
     }
     for (int s = 0; s < kSSlots; ++s) {
       ptx::mbar_init(&bars->s_full[s], 1);
@@ -944,7 +974,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
   const Waiter w{&bars->abort_flag, p.err, p.timeout_ns};
 
   if (warp == kLoaderWarp) {
-    loader_role<C>(&tmQ, &tmK, &tmV, p, smem, bars, w, lane);
+    kloader_role<C>(&tmK, p, smem, bars, w, lane);
   } else if (warp == kMmaWarp) {
     mma_s_role<C>(p, smem, bars, w, tmem, lane);
   } else if (warp < kSoftWarp0) {
@@ -953,8 +983,10 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     softmax_role<C>(p, smem, bars, w, tmem, (warp - kSoftWarp0) >> 2);
   } else if (warp == vloader_warp(C::NWG)) {
     vloader_role<C>(&tmV, p, smem, bars, w, lane);
-  } else {
+  } else if (warp == pv_warp(C::NWG)) {
     mma_pv_role<C>(p, smem, bars, w, tmem, lane);
+  } else {
+    scheduler_role<C>(&tmQ, p, smem, bars, w, lane);
   }
 
   ptx::tc_fence_before();
