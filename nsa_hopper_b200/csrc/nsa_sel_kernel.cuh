@@ -100,12 +100,16 @@ struct Params {
   int out_bufs;     // output staging tiles (2: double buffer; 1 when shared memory is tight)
 };
 
-// P tiles: two buffers.  With two softmax groups, group w always uses buffer w; with one
-// group, its k-th chunk uses buffer k & 1.  The (k)-th use of a buffer is its phase index.
-template <int NWG>
-__device__ __forceinline__ int pslot_of(int wg, uint32_t k) { return NWG == 2 ? wg : (int)(k & 1u); }
-template <int NWG>
-__device__ __forceinline__ uint32_t pphase_of(uint32_t k) { return NWG == 2 ? k : (k >> 1); }
+// P tiles: NP buffers (4 for N <= 32 and d_qk <= 128, else 2), NP / NWG per softmax group; the k-th chunk of
+// group w uses buffer w * (NP / NWG) + k % (NP / NWG), and k / (NP / NWG) is the phase index of
+// that use.  More than one buffer per group lets the softmax run a chunk ahead of the PV MMAs.
+constexpr int kMaxPSlots = 4;
+template <int NP, int NWG>
+__device__ __forceinline__ int pslot_of(int wg, uint32_t k) {
+  return wg * (NP / NWG) + (int)(k % (uint32_t)(NP / NWG));
+}
+template <int NP, int NWG>
+__device__ __forceinline__ uint32_t pphase_of(uint32_t k) { return k / (uint32_t)(NP / NWG); }
 
 struct SmemBars {
   uint64_t info_full[kInfoSlots], info_empty[kInfoSlots];
@@ -113,7 +117,7 @@ struct SmemBars {
   uint64_t k_full[kMaxStages], k_empty[kMaxStages];
   uint64_t v_full[kMaxStages], v_empty[kMaxStages];
   uint64_t s_full[kSSlots], s_empty[kSSlots];
-  uint64_t p_full[2], pv_done[2];
+  uint64_t p_full[kMaxPSlots], pv_done[kMaxPSlots];
   uint64_t o_full[2], wg_done[2], o_empty[2];
   uint64_t drain_s, drain_pv;
   uint64_t stall;  // never arrived on; only the debug_stall path waits on it
@@ -147,6 +151,7 @@ struct Cfg {
   static constexpr int kQBytes = (DQK / 64) * kQChunk;
   static constexpr int kPSub = NCOL * 128;                  // P^T for one 64-key sub-block
   static constexpr int kPBytes = 2 * kPSub;
+  static constexpr int kPSlots = (NCOL <= 32 && DQK <= 128) ? 4 : 2;  // P tiles (see pslot_of); measured best
   static constexpr int kTPC = 128 / NCOL;                   // softmax threads per query row
   static constexpr int kKPT = NCOL;                         // keys per softmax thread per chunk
   static constexpr int kTRS = kChunk + 4;                   // transpose row stride (floats)
@@ -172,7 +177,7 @@ __host__ __device__ inline SmemLayout smem_layout(int KS, int VS, int maxsub, in
   s.off_v = o; o += (uint32_t)VS * C::kVStage;
   s.off_q = o; o += (uint32_t)kQSlots * C::kQBytes;
   o = align_up(o, 1024);
-  s.off_p = o; o += 2u * C::kPBytes;
+  s.off_p = o; o += (uint32_t)C::kPSlots * C::kPBytes;
   o = align_up(o, 128);
   s.off_out = o; o += (uint32_t)out_bufs * C::kOutBytes;
   o = align_up(o, 16);
@@ -573,14 +578,14 @@ __device__ void mma_pv_role(const Params& p, uint8_t* smem, SmemBars* bars, cons
         for (int c = 0; c < nch; ++c, v.next((uint32_t)p.VS)) {
           const int wg = c % C::NWG;
           const uint32_t k = wg ? kc1++ : kc0++;
-          const int ps = pslot_of<C::NWG>(wg, k);
+          const int ps = pslot_of<C::kPSlots, C::NWG>(wg, k);
           const int nsc = min(2, nsub - 2 * c);
           const uint32_t vs = v.idx;
           const bool first = c < C::NWG;
           const uint64_t a0 = ptx::sdesc_sw128(v_base + vs * C::kVStage, C::kBox, 1024);
           const uint64_t b0 = ptx::sdesc_sw128(p_base + ps * C::kPBytes, 16, 1024);
           const uint32_t dO = tmem + C::kTmemO + (wg * 2 + (ne & 1)) * C::NCOL;
-          if (!w.wait(&bars->p_full[ps], pphase_of<C::NWG>(k) & 1)) { ok = false; break; }
+          if (!w.wait(&bars->p_full[ps], pphase_of<C::kPSlots, C::NWG>(k) & 1)) { ok = false; break; }
           if (first && ne >= 2 && !w.wait(&bars->o_empty[ne & 1], ((ne >> 1) - 1) & 1)) { ok = false; break; }
           const long long t0 = clock64();
           if (!w.wait(&bars->v_full[vs], v.phase)) { ok = false; break; }
@@ -725,7 +730,7 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, SmemBars* bars, con
       const bool any = ptx::named_bar_or(bar_id, 128, need);
       if (any) {
         // Rescale this group's O^T (lane L = d) once its previous PV (chunk k-1) has landed.
-        dead |= !w.wait(&bars->pv_done[pslot_of<NWG>(wg, k - 1)], pphase_of<NWG>(k - 1) & 1);
+        dead |= !w.wait(&bars->pv_done[pslot_of<C::kPSlots, NWG>(wg, k - 1)], pphase_of<C::kPSlots, NWG>(k - 1) & 1);
         ptx::tc_fence_after();
 #pragma unroll
         for (int h0 = 0; h0 < NCOL; h0 += 16) {
@@ -738,9 +743,9 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, SmemBars* bars, con
         }
         ptx::tmem_wait_st();
       }
-      // The P buffer was last read by this group's PV of chunk k-1 (two groups) or k-2 (one).
-      const int ps = pslot_of<NWG>(wg, k);
-      const uint32_t pph = pphase_of<NWG>(k);
+      // The P buffer was last read by this group's PV of chunk k - NP/NWG.
+      const int ps = pslot_of<C::kPSlots, NWG>(wg, k);
+      const uint32_t pph = pphase_of<C::kPSlots, NWG>(k);
       if (pph >= 1) dead |= !w.wait(&bars->pv_done[ps], (pph - 1) & 1);
 
       const float mref = (m_use == -INFINITY) ? 0.f : m_use;
@@ -934,9 +939,11 @@ __global__ void __launch_bounds__(C::kThreads, 1)
       ptx::mbar_init(&bars->q_full[s], 1);
       ptx::mbar_init(&bars->q_empty[s], 1);
     }
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kMaxPSlots; ++s) {
       ptx::mbar_init(&bars->p_full[s], 4);
       ptx::mbar_init(&bars->pv_done[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
       ptx::mbar_init(&bars->o_full[s], 1);
       ptx::mbar_init(&bars->wg_done[s], 4 * C::NWG);
       ptx::mbar_init(&bars->o_empty[s], 4);
