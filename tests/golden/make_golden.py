@@ -88,16 +88,74 @@ def store(path, name, meta, q, k, v, sel, o, lse, full):
     print("wrote", name, {k2: np.asarray(v2).shape for k2, v2 in rec.items() if k2 not in ("sha256",)})
 
 
+def nsa_full_cases(out_dir, nsa_forward, compress_kv):
+    """Full NSA forward (all three branches, the reference's own block selection) in fp64 on the
+    make_testset.py:8-18 grid, one case per shape plus the large-magnitude-row variant
+    (make_testset.py:24-25).  Besides O it stores the reference's selection and, for 256 sampled
+    (b, kvh, t), the fp64 block scores that selection ranks (nsa_reference.py:31-42, computed
+    here with the reference's compress_kv and the same tensor ops), so a selection kernel can be
+    checked up to near-ties."""
+    grid = [
+        # (B, Hq, Hkv, S, D, n_sel, l_prime, window)   make_testset.py:9-18
+        (1, 8, 2, 512, 64, 4, 64, 128),
+        (1, 8, 2, 512, 64, 16, 64, 128),
+        (2, 16, 2, 1024, 128, 8, 64, 256),
+        (1, 4, 4, 512, 64, 4, 64, 128),
+        (1, 16, 1, 768, 64, 8, 128, 256),
+        (1, 8, 2, 500, 64, 4, 64, 128),
+        (1, 8, 2, 512, 64, 1, 256, 64),
+        (1, 8, 2, 2048, 128, 16, 64, 512),
+    ]
+    cases = [(f"nsa_full_{i}", *shape, 200 + i, False) for i, shape in enumerate(grid)]
+    cases.append(("nsa_full_bigrow", *grid[0], 250, True))
+    for name, B, Hq, Hkv, S, D, n_sel, lp, w, seed, big in cases:
+        q, k, v = qkv(B, Hq, Hkv, S, D, D, seed)
+        if big:
+            q = q.clone()
+            q[..., 0, :] = (q[..., 0, :].float() * 50.0).to(torch.bfloat16)
+        o64, sel = nsa_forward(q, k, v, n_sel=n_sel, l_prime=lp, window=w, dtype=torch.float64)
+        # block scores as select_blocks ranks them (fp64)
+        G = Hq // Hkv
+        Kc, _ = compress_kv(k.double(), v.double(), 32, 16)
+        qg = q.double().view(B, Hkv, G, S, D).sum(2)
+        sc = (qg @ Kc.transpose(-1, -2)) / (D ** 0.5)
+        n_blk = (S + lp - 1) // lp
+        src = torch.linspace(0, S - 1, Kc.shape[2])
+        tgt = (src // lp).long().clamp(max=n_blk - 1)
+        blk = torch.zeros(B, Hkv, S, n_blk, dtype=torch.float64)
+        blk.index_add_(3, tgt, sc)
+        qpos = torch.arange(S).view(-1, 1)
+        bpos = torch.arange(n_blk).view(1, -1) * lp
+        blk = blk.masked_fill((bpos > qpos).view(1, 1, S, n_blk), float("-inf"))
+        rng = np.random.Generator(np.random.PCG64(77))
+        brows = np.stack([rng.integers(0, B, 256), rng.integers(0, Hkv, 256), rng.integers(0, S, 256)], 1)
+        o = o64.numpy()
+        rec = dict(kind="nsa_forward_full", B=B, Hq=Hq, Hkv=Hkv, T=S, dqk=D, dv=D, LP=lp, BQ=1, n_sel=n_sel,
+                   window=w, seed=seed, big_row=int(big), sha256=digest(q, k, v), sel=sel.numpy().astype(np.int32),
+                   checksums=checksums(o, 1234), out_absmax=np.abs(o).max(),
+                   blk_rows=brows.astype(np.int32), blk=blk.numpy()[brows[:, 0], brows[:, 1], brows[:, 2]])
+        rows = np.stack([rng.integers(0, B, 256), rng.integers(0, Hq, 256), rng.integers(0, S, 256)], 1)
+        rec["rows"] = rows.astype(np.int32)
+        rec["o_rows"] = o[rows[:, 0], rows[:, 1], rows[:, 2]].astype(np.float64)
+        np.savez_compressed(os.path.join(out_dir, name + ".npz"), **{k2: np.asarray(v2) for k2, v2 in rec.items()})
+        print("wrote", name)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="directory holding ref_only.py and nsa_reference.py")
     ap.add_argument("--out", default=HERE)
+    ap.add_argument("--only", choices=["selected", "nsa_full"], default=None, help="generate one group of fixtures")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
-    from nsa_reference import nsa_forward  # noqa: E402
+    from nsa_reference import compress_kv, nsa_forward  # noqa: E402
     from ref_only import ref_selected  # noqa: E402
 
     torch.set_num_threads(max(1, os.cpu_count() or 1))
+    if args.only != "selected":
+        nsa_full_cases(args.out, nsa_forward, compress_kv)
+    if args.only == "nsa_full":
+        return
     # ---- per-query-block selection: the reference kernel tests' shapes and rule (test_v2.py:8-20)
     qblock_cases = [
         # name, B, Hq, Hkv, S, D, KSEL, BQ, LP, seed, full

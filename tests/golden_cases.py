@@ -13,14 +13,23 @@ GOLDEN_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 
 
 def case_names() -> List[str]:
-    return sorted(os.path.splitext(os.path.basename(p))[0] for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz")))
+    """Selected-branch fixtures (ref_selected / the selected branch of nsa_forward)."""
+    return sorted(os.path.splitext(os.path.basename(p))[0] for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz"))
+                  if not os.path.basename(p).startswith("nsa_full_"))
+
+
+def full_case_names() -> List[str]:
+    """Full NSA forward fixtures (all three branches, the reference's own selection)."""
+    return sorted(os.path.splitext(os.path.basename(p))[0]
+                  for p in glob.glob(os.path.join(GOLDEN_DIR, "nsa_full_*.npz")))
 
 
 def load(name: str) -> Dict:
     z = np.load(os.path.join(GOLDEN_DIR, name + ".npz"))
     c = {k: z[k] for k in z.files}
-    for k in ("B", "Hq", "Hkv", "T", "dqk", "dv", "LP", "BQ", "seed"):
-        c[k] = int(c[k])
+    for k in ("B", "Hq", "Hkv", "T", "dqk", "dv", "LP", "BQ", "seed", "n_sel", "window"):
+        if k in c:
+            c[k] = int(c[k])
     c["big_row"] = int(c.get("big_row", 0))
     g = torch.Generator().manual_seed(c["seed"])
     q = torch.randn(c["B"], c["Hq"], c["T"], c["dqk"], generator=g).to(torch.bfloat16)
