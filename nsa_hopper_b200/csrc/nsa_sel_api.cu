@@ -95,7 +95,7 @@ typedef void (*KernelFn)(const CUtensorMap, const CUtensorMap, const CUtensorMap
 typedef nsa::SmemLayout (*LayoutFn)(int, int, int, int);
 
 struct Variant {
-  int dqk, dv, ncol, out_f32, nwg, threads;
+  int dqk, dv, ncol, out_f32, nwg, vgroups, threads;
   KernelFn kernel;
   LayoutFn layout;
   int k_stage, v_stage, tmem_cols;
@@ -109,6 +109,7 @@ Variant make_variant() {
                  NCOL,
                  sizeof(OutT) == 4 ? 1 : 0,
                  NWG,
+                 C::kVGroups,
                  C::kThreads,
                  reinterpret_cast<KernelFn>(&nsa::nsa_sel_fwd_kernel<C>),
                  &nsa::smem_layout<C>,
@@ -233,6 +234,8 @@ int make_plan(const nsa_sel_desc* d, int sm_count, Plan* pl) {
   }
   if (ks == 0) return fail(NSA_ERR_UNSUPPORTED, "tile does not fit in shared memory");
   if (ks < nsa::kMaxStages && fits(ks + 1, vs)) ++ks;
+  // With one PV warp per softmax group the V stages are split between them: keep a multiple.
+  const int vmult = V.vgroups;
   const char* env_ks = getenv("NSA_SEL_KSTAGES");
   const char* env_vs = getenv("NSA_SEL_VSTAGES");
   if (env_ks != nullptr || env_vs != nullptr) {
@@ -242,6 +245,8 @@ int make_plan(const nsa_sel_desc* d, int sm_count, Plan* pl) {
       vs = evs;
     }
   }
+  if (vmult > 1) vs -= vs % vmult;
+  if (vs < vmult) return fail(NSA_ERR_UNSUPPORTED, "tile does not fit in shared memory");
   pl->KS = ks;
   pl->VS = vs;
   pl->out_bufs = ob;

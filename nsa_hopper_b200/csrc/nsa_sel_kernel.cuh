@@ -12,29 +12,32 @@
 //    KV-head-major order, so all SMs sweep the tokens of one KV head together and the
 //    gathered K/V blocks of that head are re-read from L2 rather than HBM.  K/V loads carry
 //    an L2 evict_last hint, the streaming Q loads evict_first.
-//  * K-loader warp: turns a unit's selection row into a list of 64-key sub-blocks (dedupe,
-//    padding, causal and range clipping) in a shared-memory "info" ring and issues TMA tensor
-//    loads: the unit's Q tile (one unit ahead) and, per chunk of two sub-blocks (128 keys),
-//    the K boxes, issued from several lanes.  A V-loader warp fills the V ring the same way
-//    (one 16 KB box per sub-block).
-//  * Two MMA warps, one issuing thread each, use tcgen05 UMMAs in swap-AB form, so the 128
-//    keys of a chunk are the M=128 dimension and the G*BQ query rows of the unit are N (16..64):
+//  * Scheduler warp: turns each unit's selection row into a list of 64-key sub-blocks (set
+//    semantics, padding, causal and range clipping) in a shared-memory "info" ring and loads
+//    the unit's Q tile, running several units ahead.  The K-loader warp and the V-loader warp
+//    only wait for free ring stages and issue the K and V boxes of each 128-key chunk (two
+//    sub-blocks), one box per lane.
+//  * MMA warps, one issuing thread each, use tcgen05 UMMAs in swap-AB form, so the 128 keys of
+//    a chunk are the M=128 dimension and the G*BQ query rows of the unit are N (16..64):
 //        S^T[keys x rows]  = K_chunk[keys x d_qk] . Q^T          (A K-major, B K-major)
 //        O^T[d_v x rows]  += V_chunk^T[d_v x keys] . P^T          (A MN-major, B K-major)
-//    The score warp issues as soon as a K tile and one of four TMEM score buffers are free
-//    (running ahead of the softmax); the PV warp issues as soon as a P tile and its V tile
-//    are ready.
-//  * NWG softmax warpgroups (1 or 2): chunk g of the stream belongs to group g % NWG, which
-//    keeps its own online-softmax state and its own O^T accumulator in TMEM (a split over the
+//    The score warp runs ahead of the softmax into TMEM score buffers; there is one PV warp
+//    per softmax group, so the two groups' PV streams never queue behind each other.
+//  * NWG softmax warpgroups (1 or 2): chunk c of a unit belongs to group c % NWG, which keeps
+//    its own online-softmax state and its own O^T accumulator in TMEM (a split over the
 //    unit's keys, merged by the epilogue).  Per chunk a group reads S^T from TMEM, transposes
 //    it through shared memory so each thread owns NCOL keys of one query row, masks, runs an
 //    exp2 online softmax with a warp-shuffle row max and lazy O rescaling (only when the
 //    running max grows by more than 2^8), and writes P^T as bf16 in the UMMA K-major SW128
-//    layout.
+//    layout (two P buffers per group when they fit, so it runs a chunk ahead of its PVs).
 //  * Epilogue warpgroup: merges the groups' partial results (O, running max, sum), writes
 //    the fp32 log-sum-exp and stores O (bf16 or fp32) with TMA tensor stores, overlapping
 //    the softmax of the next unit.
 //
+// Every ring slot (score buffers, V stages, P tiles) has exactly one consumer that waits on
+// its laps in order: an mbarrier parity wait for lap L returns at once while lap L-1 is still
+// incomplete, so slots shared by two consumers in alternation would let one of them read a
+// stale tile.
 // Every mbarrier wait is bounded by %globaltimer; a wait that runs out sets an error bit,
 // all roles stop, in-flight TMA loads/stores and UMMAs are drained and TMEM is freed.
 #pragma once
@@ -50,21 +53,29 @@ constexpr int kChunk = 128;       // keys per chunk = M of the UMMAs
 constexpr int kInfoSlots = 4;     // depth of the unit-info ring
 constexpr int kInfoHdr = 16;      // ints of header per info slot
 constexpr int kMaxStages = 8;     // upper bound on K and V ring depth
-constexpr int kSSlots = 4;        // TMEM score buffers (MMA look-ahead)
+#ifndef NSA_SSLOTS
+#define NSA_SSLOTS 4
+#endif
+constexpr int kMaxSSlots = 8;     // TMEM score buffers (MMA look-ahead), split between softmax groups
 constexpr int kQSlots = 3;        // Q tile ring (the loader stages one unit ahead)
 constexpr int kLoaderWarp = 0;    // K tiles
 constexpr int kMmaWarp = 1;       // score MMAs; owns the TMEM allocation
 constexpr int kEpiWarp0 = 2;      // warps 2..5: epilogue
-constexpr int kSoftWarp0 = 6;     // warps 6..6+4*NWG-1: softmax warpgroups; then the V loader, the
-                                  // PV MMA warp and the scheduler (unit info and Q tiles)
+constexpr int kSoftWarp0 = 6;     // warps 6..6+4*NWG-1: softmax warpgroups; then the V loader, one
+                                  // PV MMA warp per softmax group and the scheduler (unit info, Q)
 constexpr uint32_t kEpiBar = 1;   // named barrier of the epilogue warpgroup
 constexpr uint32_t kWgBar0 = 2;   // named barrier of softmax warpgroup w = kWgBar0 + w
 constexpr float kRescaleLog2 = 8.0f;
 constexpr int kDevErrTimeout = 1;
 
+#ifndef NSA_SPLIT_PV
+#define NSA_SPLIT_PV 1
+#endif
+// PV MMA warps: one per softmax group when split, else one for all chunks.
+__host__ __device__ constexpr int pv_warps(int nwg) { return NSA_SPLIT_PV ? nwg : 1; }
 __host__ __device__ constexpr int vloader_warp(int nwg) { return kSoftWarp0 + 4 * nwg; }
 __host__ __device__ constexpr int pv_warp(int nwg) { return kSoftWarp0 + 4 * nwg + 1; }
-__host__ __device__ constexpr int sched_warp(int nwg) { return kSoftWarp0 + 4 * nwg + 2; }
+__host__ __device__ constexpr int sched_warp(int nwg) { return kSoftWarp0 + 4 * nwg + 1 + pv_warps(nwg); }
 __host__ __device__ constexpr int threads_for(int nwg) { return 32 * (sched_warp(nwg) + 1); }
 
 // Position in a ring of `n` slots: slot index and the parity of the lap (the mbarrier phase of
@@ -116,10 +127,10 @@ struct SmemBars {
   uint64_t q_full[kQSlots], q_empty[kQSlots];
   uint64_t k_full[kMaxStages], k_empty[kMaxStages];
   uint64_t v_full[kMaxStages], v_empty[kMaxStages];
-  uint64_t s_full[kSSlots], s_empty[kSSlots];
+  uint64_t s_full[kMaxSSlots], s_empty[kMaxSSlots];
   uint64_t p_full[kMaxPSlots], pv_done[kMaxPSlots];
   uint64_t o_full[2], wg_done[2], o_empty[2];
-  uint64_t drain_s, drain_pv;
+  uint64_t drain_s, drain_pv[2];
   uint64_t stall;  // never arrived on; only the debug_stall path waits on it
   uint32_t tmem_base;
   int abort_flag;
@@ -158,9 +169,15 @@ struct Cfg {
   static constexpr int kTrBytes = NCOL * kTRS * 4;
   static constexpr int kOutChunkElems = NCOL * 64;
   static constexpr int kOutBytes = (DV / 64) * kOutChunkElems * (int)sizeof(OutT);
+  static constexpr int kSSlots = NCOL >= 64 ? 4 : NSA_SSLOTS;  // score buffers (TMEM: 512 columns)
+  static constexpr int kSPer = kSSlots / NWG;               // score buffers per softmax group
+  static constexpr int kPvWarps = pv_warps(NWG);
+  static constexpr int kVGroups = kPvWarps;                 // V stages are split between PV warps
   static constexpr int kTmemS = 0;                          // score buffers: kSSlots x NCOL columns
   static constexpr int kTmemO = kSSlots * NCOL;             // O^T accumulators: [wg][unit parity] x NCOL
   static constexpr int kTmemCols = ceil_pow2_32((kSSlots + 2 * NWG) * NCOL);
+  static_assert(kTmemCols <= 512, "TMEM holds 512 columns");
+  static_assert(kSSlots <= kMaxSSlots && kSSlots % NWG == 0, "score buffers");
   static constexpr uint32_t kIdescS = ptx::idesc_bf16_f32(128, NCOL, false, false);
   static constexpr uint32_t kIdescPV = ptx::idesc_bf16_f32(128, NCOL, true, false);
 };
@@ -449,7 +466,8 @@ __device__ void vloader_role(const CUtensorMap* tmV, const Params& p, uint8_t* s
                              const Waiter& w, int lane) {
   const uint64_t pol_kv = ptx::policy_evict_last();
   uint8_t* vdst0 = smem + p.off_v + lane * C::kVSub;
-  Ring info, v;
+  const uint32_t vper = (uint32_t)(p.VS / C::kVGroups);  // V stages per PV warp
+  Ring info, v0, v1;  // V stage ring of PV warp 0 / 1
   bool ok = true;
   for (int u = blockIdx.x; u < p.n_units && ok; u += gridDim.x) {
     int got = 1;
@@ -463,38 +481,44 @@ __device__ void vloader_role(const CUtensorMap* tmV, const Params& p, uint8_t* s
       const int nsc = min(2, nsub - 2 * c);
       const bool mine = lane < nsc;
       const int row = mine ? inf[kInfoHdr + 2 * c + lane] : 0;
-      uint8_t* dst = vdst0 + v.idx * C::kVStage;
+      const bool g1 = C::kVGroups > 1 && (c & 1);
+      const Ring v = g1 ? v1 : v0;
+      const uint32_t vs = (g1 ? vper : 0u) + v.idx;
+      uint8_t* dst = vdst0 + vs * C::kVStage;
       int go = 1;
       if (lane == 0) {
-        go = (!v.lapped || w.wait(&bars->v_empty[v.idx], v.phase ^ 1u)) ? 1 : 0;
-        if (go) ptx::mbar_arrive_expect_tx(&bars->v_full[v.idx], (uint32_t)(nsc * kSub * C::DV * 2));
+        go = (!v.lapped || w.wait(&bars->v_empty[vs], v.phase ^ 1u)) ? 1 : 0;
+        if (go) ptx::mbar_arrive_expect_tx(&bars->v_full[vs], (uint32_t)(nsc * kSub * C::DV * 2));
       }
       if (!__shfl_sync(0xffffffffu, go, 0)) { ok = false; break; }
-      if (mine) ptx::tma_load_4d(dst, tmV, &bars->v_full[v.idx], 0, row, 0, bkv, pol_kv);
-      v.next((uint32_t)p.VS);
+      if (mine) ptx::tma_load_4d(dst, tmV, &bars->v_full[vs], 0, row, 0, bkv, pol_kv);
+      if (g1) v1.next(vper); else v0.next(vper);
     }
     if (ok && lane == 0) ptx::mbar_arrive(&bars->info_empty[info.idx]);
     info.next(kInfoSlots);
   }
   // Drain: the most recent load of every stage has landed.
   if (lane == 0) {
-    for (int s2 = 0; s2 < p.VS; ++s2) {
-      const uint32_t back = (uint32_t)s2 + 1u;
-      const uint32_t slot = (v.idx + (uint32_t)p.VS - back % (uint32_t)p.VS) % (uint32_t)p.VS;
-      const uint32_t ph = (v.idx >= back) ? v.phase : (v.phase ^ 1u);
-      if (v.lapped || v.idx >= back) w.wait_drain(&bars->v_full[slot], ph);
+    for (int wg = 0; wg < C::kVGroups; ++wg) {
+      const Ring v = wg ? v1 : v0;
+      for (uint32_t back = 1; back <= vper; ++back) {
+        const uint32_t slot = (v.idx + vper - back % vper) % vper;
+        const uint32_t ph = (v.idx >= back) ? v.phase : (v.phase ^ 1u);
+        if (v.lapped || v.idx >= back) w.wait_drain(&bars->v_full[wg * vper + slot], ph);
+      }
     }
   }
   __syncwarp();
 }
 
 // ------------------------------------------------------------------------------------------
-// MMA issue.  Two warps each issue one stream from one thread, in ring order, with blocking
+// MMA issue.  Each MMA warp issues one stream from one thread, in ring order, with blocking
 // (bounded) waits:
-//   score warp: S_g = K_g . Q^T into TMEM score buffer g % 4 as soon as K_g has landed and the
-//               softmax has read the buffer's previous chunk (so it runs ahead of the softmax);
-//   PV warp:    O^T += V_g^T . P_g^T into the owning group's accumulator as soon as P_g and V_g
-//               are ready.
+//   score warp: S = K_chunk . Q^T into the next score buffer of the chunk's softmax group as
+//               soon as the K tile has landed and the group has read that buffer's previous
+//               chunk (so it runs ahead of the softmax);
+//   PV warp w:  O^T += V_chunk^T . P^T into group w's accumulator as soon as the group's P tile
+//               and its V stage are ready.
 // Shared-memory descriptors are built once per tile; each 16-wide K step adds a constant.
 // ------------------------------------------------------------------------------------------
 __device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t byte_off) { return d + (uint64_t)(byte_off >> 4); }
@@ -505,8 +529,9 @@ __device__ void mma_s_role(const Params& p, uint8_t* smem, SmemBars* bars, const
     bool ok = true;
     // Error-path test hook: a bounded wait that can only end by running out of time.
     if (p.debug_stall) ok = w.wait(&bars->stall, 0);
-    uint32_t g = 0, ui = 0, ne = 0;
+    uint32_t ui = 0, ne = 0;
     Ring k;
+    uint32_t sc0 = 0, sc1 = 0;  // chunks issued so far for softmax group 0 / 1 (their score buffers)
     const uint32_t k_base = ptx::smem_u32(smem + p.off_k);
     const uint32_t q_base = ptx::smem_u32(smem + p.off_q);
     for (int u = blockIdx.x; u < p.n_units && ok; u += gridDim.x, ++ui) {
@@ -521,11 +546,14 @@ __device__ void mma_s_role(const Params& p, uint8_t* smem, SmemBars* bars, const
         long long t_wait = 0;
         if (!w.wait(&bars->q_full[qs], (ne / kQSlots) & 1)) break;
         const uint64_t bq0 = ptx::sdesc_sw128(q_base + qs * C::kQBytes, 16, 1024);
-        for (int c = 0; c < nch; ++c, ++g, k.next((uint32_t)p.KS)) {
-          const int sslot = g % kSSlots;
+        for (int c = 0; c < nch; ++c, k.next((uint32_t)p.KS)) {
+          const bool g1 = C::NWG == 2 && (c & 1);
+          const uint32_t scnt = g1 ? sc1 : sc0;  // the group's score buffers: its own ring
+          const int sslot = (g1 ? C::kSPer : 0) + (int)(scnt % (uint32_t)C::kSPer);
           const uint32_t ks = k.idx;
           const uint64_t a0 = ptx::sdesc_sw128(k_base + ks * C::kKStage, 16, 1024);
-          if (g >= (uint32_t)kSSlots && !w.wait(&bars->s_empty[sslot], ((g / kSSlots) - 1) & 1)) { ok = false; break; }
+          if (scnt >= (uint32_t)C::kSPer &&
+              !w.wait(&bars->s_empty[sslot], ((scnt / (uint32_t)C::kSPer) - 1u) & 1u)) { ok = false; break; }
           const long long t0 = clock64();
           if (!w.wait(&bars->k_full[ks], k.phase)) { ok = false; break; }
           t_wait += clock64() - t0;
@@ -539,6 +567,7 @@ __device__ void mma_s_role(const Params& p, uint8_t* smem, SmemBars* bars, const
           }
           ptx::umma_commit(&bars->k_empty[ks]);
           ptx::umma_commit(&bars->s_full[sslot]);
+          if (g1) ++sc1; else ++sc0;
         }
         if (!ok) break;
         ptx::umma_commit(&bars->q_empty[qs]);
@@ -555,14 +584,17 @@ __device__ void mma_s_role(const Params& p, uint8_t* smem, SmemBars* bars, const
   __syncwarp();
 }
 
+// PV warp `mine` issues the PV MMAs of softmax group `mine`'s chunks (all chunks with one group),
+// so the two groups' PV streams do not queue behind each other.
 template <class C>
 __device__ void mma_pv_role(const Params& p, uint8_t* smem, SmemBars* bars, const Waiter& w, uint32_t tmem,
-                            int lane) {
+                            int lane, int mine) {
   if (lane == 0) {
     bool ok = true;
     uint32_t ui = 0, ne = 0;
-    Ring v;
-    uint32_t kc0 = 0, kc1 = 0;  // chunks so far of softmax group 0 / 1
+    Ring v;                    // this warp's V stages
+    uint32_t kw0 = 0, kw1 = 0;  // chunks so far of softmax group 0 / 1
+    const uint32_t vper = (uint32_t)(p.VS / C::kVGroups);
     const uint32_t v_base = ptx::smem_u32(smem + p.off_v);
     const uint32_t p_base = ptx::smem_u32(smem + p.off_p);
     for (int u = blockIdx.x; u < p.n_units && ok; u += gridDim.x, ++ui) {
@@ -575,18 +607,21 @@ __device__ void mma_pv_role(const Params& p, uint8_t* smem, SmemBars* bars, cons
       if (nch > 0) {
         const long long t_unit0 = clock64();
         long long t_wait = 0;
-        for (int c = 0; c < nch; ++c, v.next((uint32_t)p.VS)) {
+        // The unit's O^T buffers were last read by the epilogue for unit ne-2.  Every PV warp
+        // waits, even one without chunks in this unit: its o_full commit below must not complete
+        // the phase of an earlier unit that the other PV warp is still accumulating.
+        if (ne >= 2 && !w.wait(&bars->o_empty[ne & 1], ((ne >> 1) - 1) & 1)) break;
+        for (int c = mine; c < nch; c += C::kPvWarps) {
           const int wg = c % C::NWG;
-          const uint32_t k = wg ? kc1++ : kc0++;
+          const uint32_t k = wg ? kw1 : kw0;
           const int ps = pslot_of<C::kPSlots, C::NWG>(wg, k);
           const int nsc = min(2, nsub - 2 * c);
-          const uint32_t vs = v.idx;
+          const uint32_t vs = (uint32_t)mine * vper + v.idx;
           const bool first = c < C::NWG;
           const uint64_t a0 = ptx::sdesc_sw128(v_base + vs * C::kVStage, C::kBox, 1024);
           const uint64_t b0 = ptx::sdesc_sw128(p_base + ps * C::kPBytes, 16, 1024);
           const uint32_t dO = tmem + C::kTmemO + (wg * 2 + (ne & 1)) * C::NCOL;
           if (!w.wait(&bars->p_full[ps], pphase_of<C::kPSlots, C::NWG>(k) & 1)) { ok = false; break; }
-          if (first && ne >= 2 && !w.wait(&bars->o_empty[ne & 1], ((ne >> 1) - 1) & 1)) { ok = false; break; }
           const long long t0 = clock64();
           if (!w.wait(&bars->v_full[vs], v.phase)) { ok = false; break; }
           t_wait += clock64() - t0;
@@ -601,10 +636,12 @@ __device__ void mma_pv_role(const Params& p, uint8_t* smem, SmemBars* bars, cons
           }
           ptx::umma_commit(&bars->v_empty[vs]);
           ptx::umma_commit(&bars->pv_done[ps]);
+          if (wg) ++kw1; else ++kw0;
+          v.next(vper);
         }
         if (!ok) break;
         ptx::umma_commit(&bars->o_full[ne & 1]);
-        if (p.cyc != nullptr) {
+        if (p.cyc != nullptr && mine == 0) {
           const long long tot = clock64() - t_unit0;
           atomicAdd(reinterpret_cast<unsigned long long*>(p.cyc + 2 * (size_t)ref), (unsigned long long)t_wait);
           atomicAdd(reinterpret_cast<unsigned long long*>(p.cyc + 2 * (size_t)ref + 1),
@@ -614,8 +651,8 @@ __device__ void mma_pv_role(const Params& p, uint8_t* smem, SmemBars* bars, cons
       }
       ptx::mbar_arrive(&bars->info_empty[slot]);
     }
-    ptx::umma_commit(&bars->drain_pv);
-    w.wait_drain(&bars->drain_pv, 0);
+    ptx::umma_commit(&bars->drain_pv[mine]);
+    w.wait_drain(&bars->drain_pv[mine], 0);
   }
   __syncwarp();
 }
@@ -641,7 +678,7 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, SmemBars* bars, con
   const int nrows = p.G * p.BQs;
   const bool col_real = col < nrows;
   const int col_i = col - (col / p.BQs) * p.BQs;
-  uint32_t ui = 0, ne = 0, g = 0, k = 0;  // k: chunks this group has processed
+  uint32_t ui = 0, ne = 0, k = 0;  // k: chunks this group has processed (also its score-buffer ring)
   bool dead = false;
 
   for (int u = blockIdx.x; u < p.n_units; u += gridDim.x, ++ui) {
@@ -662,9 +699,8 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, SmemBars* bars, con
     bool first = true, quit = false;
 
     for (int c = wg; c < nch; c += NWG) {
-      const uint32_t gg = g + c;
-      const int sslot = gg % kSSlots;
-      dead |= !w.wait(&bars->s_full[sslot], (gg / kSSlots) & 1);
+      const int sslot = wg * C::kSPer + (int)(k % (uint32_t)C::kSPer);
+      dead |= !w.wait(&bars->s_full[sslot], (k / (uint32_t)C::kSPer) & 1u);
       ptx::tc_fence_after();
       {
         const uint32_t saddr = tmem + lane_addr + C::kTmemS + sslot * NCOL;
@@ -781,7 +817,6 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, SmemBars* bars, con
       ++k;
     }
     if (quit) break;
-    g += nch;
 
     // Publish this group's running max and sum for the epilogue's merge.  The slot of unit
     // ne was last read by the epilogue for unit ne-2 (it arrives on o_empty after that).
@@ -929,9 +964,10 @@ __global__ void __launch_bounds__(C::kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kInfoSlots; ++s) {
       ptx::mbar_init(&bars->info_full[s], 1);
-      ptx::mbar_init(&bars->info_empty[s], 5 + C::NWG);  // 2 MMA warps, K and V loaders, epilogue, softmax groups
+      // consumers: score MMA, K and V loaders, epilogue, the softmax groups and the PV warps
+      ptx::mbar_init(&bars->info_empty[s], 4 + C::NWG + C::kPvWarps);
     }
-    for (int s = 0; s < kSSlots; ++s) {
+    for (int s = 0; s < C::kSSlots; ++s) {
       ptx::mbar_init(&bars->s_full[s], 1);
       ptx::mbar_init(&bars->s_empty[s], 4);
     }
@@ -944,7 +980,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
       ptx::mbar_init(&bars->pv_done[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
-      ptx::mbar_init(&bars->o_full[s], 1);
+      ptx::mbar_init(&bars->o_full[s], C::kPvWarps);  // each PV warp commits once per unit
       ptx::mbar_init(&bars->wg_done[s], 4 * C::NWG);
       ptx::mbar_init(&bars->o_empty[s], 4);
     }
@@ -955,7 +991,8 @@ __global__ void __launch_bounds__(C::kThreads, 1)
       ptx::mbar_init(&bars->v_empty[s], 1);
     }
     ptx::mbar_init(&bars->drain_s, 1);
-    ptx::mbar_init(&bars->drain_pv, 1);
+    ptx::mbar_init(&bars->drain_pv[0], 1);
+    ptx::mbar_init(&bars->drain_pv[1], 1);
     ptx::mbar_init(&bars->stall, 1);
     bars->abort_flag = 0;
     ptx::fence_mbar_init();
@@ -990,8 +1027,8 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     softmax_role<C>(p, smem, bars, w, tmem, (warp - kSoftWarp0) >> 2);
   } else if (warp == vloader_warp(C::NWG)) {
     vloader_role<C>(&tmV, p, smem, bars, w, lane);
-  } else if (warp == pv_warp(C::NWG)) {
-    mma_pv_role<C>(p, smem, bars, w, tmem, lane);
+  } else if (warp < sched_warp(C::NWG)) {
+    mma_pv_role<C>(p, smem, bars, w, tmem, lane, warp - pv_warp(C::NWG));
   } else {
     scheduler_role<C>(&tmQ, p, smem, bars, w, lane);
   }
