@@ -126,6 +126,28 @@ int nsa_sel_run(const nsa_sel_desc* desc, nsa_stream_t stream);
    sm_count <= 0 means "query the current device". */
 int nsa_sel_plan(const nsa_sel_desc* desc, int32_t sm_count, nsa_sel_plan_info* out);
 
+/* Block selection: the producer of the selected branch's index rows (replaces the PyTorch
+   select_blocks of reference nsa_reference.py:27-44, with compress_kv :5-16 and the group-summed
+   queries of :70-71).  For every (b, kvh, token t) it scores selection block nb as
+       s(t, nb) = (sum_g q[b, kvh*G + g, t, :]) . kblk[b, kvh, nb, :],
+       kblk[nb] = 1/sqrt(d) * sum over compressed keys i of block nb of
+                  mean_{j < cmp_block} k[b, kvh, i*cmp_stride + j, :],
+   where compressed key i belongs to block floor(linspace(0, T-1, n_cmp)[i] / l_prime) (float32,
+   clamped to the last block; n_cmp = (T - cmp_block) / cmp_stride + 1), and writes
+       sel_out int32 [B, Hkv, T, k],  k = min(n_sel, ceil(T / l_prime)) <= 32,
+   the k best visible blocks (nb * l_prime <= t) by score, highest first; -1 where fewer than k
+   blocks are visible (the reference's topk returns masked future blocks there, which the
+   selected branch ignores in the same way).  Scores are fp32.  q, k bf16 as in nsa_sel_forward
+   (d_qk = d); kblk_workspace: caller-owned fp32 buffer of nsa_sel_select_workspace_bytes()
+   bytes, 16-byte aligned.  Two kernel launches on `stream`. */
+int nsa_sel_select(const void* q, const void* k, float* kblk_workspace, int32_t* sel_out, int32_t B, int32_t Hq,
+                   int32_t Hkv, int32_t T, int32_t d, int32_t l_prime, int32_t n_sel, int32_t cmp_block,
+                   int32_t cmp_stride, nsa_stream_t stream);
+
+/* Bytes of the workspace nsa_sel_select needs (B * Hkv * ceil(T / l_prime) * d * 4), -1 if
+   an argument is not positive. */
+int64_t nsa_sel_select_workspace_bytes(int32_t B, int32_t Hkv, int32_t T, int32_t d, int32_t l_prime);
+
 /* Text of the last error on this host thread ("" if none). */
 const char* nsa_sel_last_error(void);
 

@@ -90,6 +90,10 @@ def load(path: Optional[str] = None) -> ctypes.CDLL:
     lib.nsa_sel_last_error.restype = ctypes.c_char_p
     lib.nsa_sel_version.argtypes = []
     lib.nsa_sel_version.restype = i32
+    lib.nsa_sel_select.argtypes = [vp, vp, vp, vp] + [i32] * 9 + [vp]
+    lib.nsa_sel_select.restype = ctypes.c_int
+    lib.nsa_sel_select_workspace_bytes.argtypes = [i32] * 5
+    lib.nsa_sel_select_workspace_bytes.restype = ctypes.c_int64
     if path is None:
         _lib = lib
     return lib
@@ -129,3 +133,15 @@ def plan(desc: NsaSelDesc, sm_count: int = 148) -> Dict[str, int]:
     info = NsaSelPlanInfo()
     check(load().nsa_sel_plan(ctypes.byref(desc), sm_count, ctypes.byref(info)))
     return {name: getattr(info, name) for name, _ in NsaSelPlanInfo._fields_ if name != "reserved"}
+
+
+def select_workspace_bytes(B: int, Hkv: int, T: int, d: int, l_prime: int) -> int:
+    return int(load().nsa_sel_select_workspace_bytes(B, Hkv, T, d, l_prime))
+
+
+def select(q: int, k: int, workspace: int, sel_out: int, B: int, Hq: int, Hkv: int, T: int, d: int, l_prime: int,
+           n_sel: int, cmp_block: int = 32, cmp_stride: int = 16, stream: int = 0) -> None:
+    """nsa_sel_select on device pointers (see include/nsa_sel.h)."""
+    check(load().nsa_sel_select(ctypes.c_void_p(q), ctypes.c_void_p(k), ctypes.c_void_p(workspace),
+                                ctypes.c_void_p(sel_out), B, Hq, Hkv, T, d, l_prime, n_sel, cmp_block, cmp_stride,
+                                ctypes.c_void_p(stream)))

@@ -19,6 +19,7 @@
 
 #include "nsa_sel.h"
 #include "nsa_sel_kernel.cuh"
+#include "nsa_select_kernel.cuh"
 
 namespace {
 
@@ -392,7 +393,77 @@ int launch(const nsa_sel_desc* d, nsa_stream_t stream) {
 
 }  // namespace
 
+namespace {
+// ------------------------------------------------------------------ block selection
+int select_shape(int32_t B, int32_t Hq, int32_t Hkv, int32_t T, int32_t d, int32_t l_prime, int32_t n_sel,
+                 int32_t cmp_block, int32_t cmp_stride, int* n_blk, int* topk, int* n_cmp) {
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || T <= 0 || d <= 0 || l_prime <= 0 || n_sel <= 0 || cmp_block <= 0 ||
+      cmp_stride <= 0)
+    return fail(NSA_ERR_INVALID_ARG, "B, Hq, Hkv, T, d, l_prime, n_sel, cmp_block and cmp_stride must be positive");
+  if (Hq % Hkv != 0) return fail(NSA_ERR_INVALID_ARG, "Hq (%d) must be a multiple of Hkv (%d)", Hq, Hkv);
+  if (d % 4 != 0 || d > nsa::select::kMaxD) return fail(NSA_ERR_UNSUPPORTED, "d=%d: selection supports d % 4 == 0, d <= %d", d, nsa::select::kMaxD);
+  if ((long long)B * Hkv > 65535) return fail(NSA_ERR_UNSUPPORTED, "B*Hkv exceeds 65535");
+  if ((long long)B * Hq * T * d >= (1ll << 40)) return fail(NSA_ERR_UNSUPPORTED, "problem too large");
+  *n_blk = (T + l_prime - 1) / l_prime;
+  *topk = n_sel < *n_blk ? n_sel : *n_blk;
+  if (*topk > nsa::select::kMaxK) return fail(NSA_ERR_UNSUPPORTED, "top-k of %d exceeds %d", *topk, nsa::select::kMaxK);
+  *n_cmp = T >= cmp_block ? (T - cmp_block) / cmp_stride + 1 : 0;
+  return NSA_OK;
+}
+
+}  // namespace
+
 extern "C" {
+
+int64_t nsa_sel_select_workspace_bytes(int32_t B, int32_t Hkv, int32_t T, int32_t d, int32_t l_prime) {
+  if (B <= 0 || Hkv <= 0 || T <= 0 || d <= 0 || l_prime <= 0) return -1;
+  const int64_t n_blk = (T + l_prime - 1) / l_prime;
+  return (int64_t)B * Hkv * n_blk * d * (int64_t)sizeof(float);
+}
+
+int nsa_sel_select(const void* q, const void* k, float* kblk_workspace, int32_t* sel_out, int32_t B, int32_t Hq,
+                   int32_t Hkv, int32_t T, int32_t d, int32_t l_prime, int32_t n_sel, int32_t cmp_block,
+                   int32_t cmp_stride, nsa_stream_t stream) {
+  if (q == nullptr || k == nullptr || kblk_workspace == nullptr || sel_out == nullptr)
+    return fail(NSA_ERR_INVALID_ARG, "q, k, kblk_workspace and sel_out must be non-NULL");
+  if ((reinterpret_cast<uintptr_t>(kblk_workspace) & 15u) != 0)
+    return fail(NSA_ERR_INVALID_ARG, "kblk_workspace must be 16-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(q) & 1u) != 0 || (reinterpret_cast<uintptr_t>(k) & 1u) != 0 ||
+      (reinterpret_cast<uintptr_t>(sel_out) & 3u) != 0)
+    return fail(NSA_ERR_INVALID_ARG, "q, k and sel_out must be aligned to their element size");
+  int n_blk = 0, topk = 0, n_cmp = 0;
+  int rc = select_shape(B, Hq, Hkv, T, d, l_prime, n_sel, cmp_block, cmp_stride, &n_blk, &topk, &n_cmp);
+  if (rc != NSA_OK) return rc;
+  int sm = 0, dev = 0;
+  rc = current_sm_count(&sm, &dev);
+  if (rc != NSA_OK) return rc;
+  const int smem = (2 * nsa::select::kTile * (d + 4) + nsa::select::kTile * (nsa::select::kChunk + 1)) * 4;
+  {
+    std::lock_guard<std::mutex> lk(g_dev.mu);
+    const uint64_t bit = 1ull << 63;
+    if ((g_dev.attr_done[dev] & bit) == 0) {
+      cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(&nsa::select::select_kernel),
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (2 * nsa::select::kTile * (nsa::select::kMaxD + 4) +
+                                            nsa::select::kTile * (nsa::select::kChunk + 1)) * 4);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(select max dynamic smem)");
+      g_dev.attr_done[dev] |= bit;
+    }
+  }
+  const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const float scale = (float)(1.0 / ((double)cmp_block * sqrt((double)d)));
+  nsa::select::kblk_kernel<<<dim3(n_blk, B * Hkv), d, 0, st>>>(static_cast<const bf16*>(k), kblk_workspace, T, d,
+                                                               n_blk, n_cmp, l_prime, cmp_block, cmp_stride, scale);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "block-key kernel launch");
+  nsa::select::select_kernel<<<dim3((T + nsa::select::kTile - 1) / nsa::select::kTile, B * Hkv),
+                               nsa::select::kThreads, smem, st>>>(static_cast<const bf16*>(q), kblk_workspace, sel_out,
+                                                                  Hq, Hkv, T, d, n_blk, l_prime, topk);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "selection kernel launch");
+  g_last_error[0] = '\0';
+  return NSA_OK;
+}
 
 int nsa_sel_run(const nsa_sel_desc* desc, nsa_stream_t stream) { return launch(desc, stream); }
 

@@ -16,6 +16,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
 
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <mutex>
@@ -43,6 +44,8 @@ struct Api {
   decltype(&nsa_sel_run) run = nullptr;
   decltype(&nsa_sel_last_error) last_error = nullptr;
   decltype(&nsa_sel_version) version = nullptr;
+  decltype(&nsa_sel_select) select = nullptr;
+  decltype(&nsa_sel_select_workspace_bytes) select_ws = nullptr;
 };
 
 std::string dir_of(const std::string& path) {
@@ -73,8 +76,10 @@ const Api& api() {
     a.run = reinterpret_cast<decltype(a.run)>(dlsym(h, "nsa_sel_run"));
     a.last_error = reinterpret_cast<decltype(a.last_error)>(dlsym(h, "nsa_sel_last_error"));
     a.version = reinterpret_cast<decltype(a.version)>(dlsym(h, "nsa_sel_version"));
+    a.select = reinterpret_cast<decltype(a.select)>(dlsym(h, "nsa_sel_select"));
+    a.select_ws = reinterpret_cast<decltype(a.select_ws)>(dlsym(h, "nsa_sel_select_workspace_bytes"));
   });
-  if (!(a.forward && a.run && a.last_error && a.version))
+  if (!(a.forward && a.run && a.last_error && a.version && a.select && a.select_ws))
     TORCH_CHECK(false, format_msg("libnsa_sel.so could not be loaded (build it first): %s", error.c_str()));
   return a;
 }
@@ -166,6 +171,31 @@ std::vector<torch::Tensor> forward_lse(torch::Tensor Q, torch::Tensor K, torch::
   return {O, L};
 }
 
+// Block selection (nsa_sel_select): sel int32 [B, Hkv, T, min(n_sel, ceil(T/l_prime))].
+torch::Tensor select_blocks(torch::Tensor Q, torch::Tensor K, int64_t n_sel, int64_t l_prime, int64_t cmp_block,
+                            int64_t cmp_stride) {
+  TORCH_CHECK(Q.is_cuda() && K.is_cuda(), "Q and K must be CUDA tensors");
+  TORCH_CHECK(Q.scalar_type() == at::kBFloat16 && K.scalar_type() == at::kBFloat16, "Q and K must be bfloat16");
+  TORCH_CHECK(Q.dim() == 4 && K.dim() == 4, "expected Q [B,Hq,T,d] and K [B,Hkv,T,d]");
+  TORCH_CHECK(Q.is_contiguous() && K.is_contiguous(), "Q and K must be contiguous");
+  TORCH_CHECK(K.size(0) == Q.size(0) && K.size(2) == Q.size(2) && K.size(3) == Q.size(3), "Q/K shape mismatch");
+  const Api& a = api();
+  const c10::cuda::CUDAGuard guard(Q.device());
+  const int32_t B = i32(Q.size(0), "B"), Hq = i32(Q.size(1), "Hq"), Hkv = i32(K.size(1), "Hkv");
+  const int32_t T = i32(Q.size(2), "T"), d = i32(Q.size(3), "d"), lp = i32(l_prime, "l_prime");
+  const int64_t ws = a.select_ws(B, Hkv, T, d, lp);
+  if (ws < 0) TORCH_CHECK(false, "invalid selection shape");
+  const int64_t n_blk = (T + lp - 1) / lp;
+  const int64_t k = std::min<int64_t>(n_sel, n_blk);
+  auto work = torch::empty({std::max<int64_t>(ws / 4, 1)}, Q.options().dtype(torch::kFloat32));
+  auto sel = torch::empty({Q.size(0), K.size(1), Q.size(2), std::max<int64_t>(k, 1)}, Q.options().dtype(torch::kInt));
+  const int rc = a.select(Q.data_ptr(), K.data_ptr(), work.data_ptr<float>(), sel.data_ptr<int32_t>(), B, Hq, Hkv, T, d,
+                          lp, i32(n_sel, "n_sel"), i32(cmp_block, "cmp_block"), i32(cmp_stride, "cmp_stride"),
+                          reinterpret_cast<nsa_stream_t>(c10::cuda::getCurrentCUDAStream().stream()));
+  if (rc != NSA_OK) TORCH_CHECK(false, format_msg("nsa_sel_select failed (%d): %s", rc, a.last_error()));
+  return sel;
+}
+
 int64_t library_version() { return api().version(); }
 
 }  // namespace
@@ -176,5 +206,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("forward_lse", &forward_lse, "forward_lse(Q, K, V, sel, l_prime, BQ, cu_seqlens, scale, out_f32) -> [O, LSE]",
         py::arg("Q"), py::arg("K"), py::arg("V"), py::arg("sel"), py::arg("l_prime"), py::arg("BQ"),
         py::arg("cu_seqlens") = py::none(), py::arg("scale") = 0.0, py::arg("out_f32") = false);
+  m.def("select_blocks", &select_blocks, "select_blocks(Q, K, n_sel, l_prime, cmp_block, cmp_stride) -> sel int32",
+        py::arg("Q"), py::arg("K"), py::arg("n_sel"), py::arg("l_prime"), py::arg("cmp_block") = 32,
+        py::arg("cmp_stride") = 16);
   m.def("library_version", &library_version);
 }

@@ -1,0 +1,237 @@
+// NSA block selection for B200: the producer of the selected branch's index rows.
+//
+// What it computes (reference nsa_reference.py:27-44 with compress_kv :5-16 and the
+// group-summed queries of :70-71): for every (batch b, KV head kvh, token t)
+//     s(t, nb) = (sum_g q[b, kvh*G+g, t, :]) . kblk[b, kvh, nb, :]
+//     kblk[nb]  = (1/sqrt(d)) * sum over the compressed keys i mapped to block nb of
+//                 mean_{j < cmp_block} k[b, kvh, i*cmp_stride + j, :]
+// (the reference sums the per-compressed-key scores into their block; the score is linear in
+// the key, so summing the keys first gives the same value), visible iff nb * l_prime <= t,
+// and writes the top-k blocks (k = min(n_sel, n_blk) <= 32) by score, highest first, -1 where
+// fewer than k blocks are visible.
+//
+// Two kernels:
+//  * kblk_kernel: one CTA per (block, b*Hkv), one thread per dimension, fp32 accumulation.
+//  * select_kernel: one CTA per (64-token tile, b*Hkv), 256 threads.  The group-summed query
+//    tile (fp32) stays in shared memory; block-key tiles of 64 blocks stream through shared
+//    memory; each thread computes a 4 x 4 register tile of scores (fp32 FMA: the ranking must
+//    agree with the reference's fp64 one except at near-ties, which bf16 or tf32 tensor-core
+//    products would not).  Each warp keeps, for 8 tokens, the running top-32 (score, block) in
+//    registers, one entry per lane, sorted by a warp-wide bitonic network; a chunk of
+//    candidates is merged only if one of them beats the current k-th score.
+#pragma once
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include <math.h>
+
+namespace nsa {
+namespace select {
+
+constexpr int kTile = 64;       // tokens per CTA
+constexpr int kChunk = 64;      // blocks per shared-memory chunk
+constexpr int kThreads = 256;
+constexpr int kMaxK = 32;       // top-k capacity (one list entry per lane)
+constexpr int kMaxD = 256;
+
+// Selection block of compressed key i: floor(linspace(0, T-1, n_cmp)[i] / l_prime), clamped to
+// n_blk - 1 (nsa_reference.py:35-36).  The float32 linspace value is formed as PyTorch's CPU
+// kernel forms it (step rounded to float32, value computed in double from the nearer end, then
+// rounded) and the floor division follows PyTorch's float floor-divide; explicit _rn
+// intrinsics keep the compiler from fusing the products into FMAs.
+__device__ __forceinline__ float linspace_f32(int i, int T, int n) {
+  if (n == 1) return 0.f;
+  const float step = __fdiv_rn((float)(T - 1), (float)(n - 1));
+  if (i < n / 2) return (float)__dmul_rn((double)step, (double)i);
+  return (float)__dsub_rn((double)(T - 1), __dmul_rn((double)step, (double)(n - 1 - i)));
+}
+__device__ __forceinline__ float floor_div_f32(float a, float b) {
+  const float mod = fmodf(a, b);
+  float div = __fdiv_rn(__fsub_rn(a, mod), b);
+  if (mod != 0.f && ((b < 0.f) != (mod < 0.f))) div = __fsub_rn(div, 1.f);
+  if (div != 0.f) {
+    float fl = floorf(div);
+    if (__fsub_rn(div, fl) > 0.5f) fl = __fadd_rn(fl, 1.f);
+    return fl;
+  }
+  return copysignf(0.f, __fdiv_rn(a, b));
+}
+__device__ __forceinline__ int cmp_block_of(int i, int T, int n_cmp, int l_prime, int n_blk) {
+  const int nb = (int)floor_div_f32(linspace_f32(i, T, n_cmp), (float)l_prime);
+  return nb < n_blk - 1 ? nb : n_blk - 1;
+}
+
+// kblk[bh, nb, :] = scale * sum over compressed keys i of block nb of sum_j k[bh, i*stride + j, :]
+// (scale = 1 / (cmp_block * sqrt(d))).  One CTA per (block, b*Hkv), one thread per dimension.
+__global__ void kblk_kernel(const __nv_bfloat16* __restrict__ k, float* __restrict__ kblk, int T, int d, int n_blk,
+                            int n_cmp, int l_prime, int cmp_block, int cmp_stride, float scale) {
+  const int nb = blockIdx.x, bh = blockIdx.y, dd = threadIdx.x;
+  if (dd >= d) return;
+  // compressed keys whose linspace position falls in block nb: a window around the estimate,
+  // each candidate checked exactly (the last block also takes everything clamped into it)
+  int lo = 0, hi = 0;
+  if (n_cmp > 0) {
+    const double per = (n_cmp > 1) ? (double)(n_cmp - 1) / (double)(T - 1) : 0.0;
+    lo = max(0, (int)floor((double)nb * l_prime * per) - 2);
+    hi = (nb == n_blk - 1) ? n_cmp : min(n_cmp, (int)ceil((double)(nb + 1) * l_prime * per) + 3);
+  }
+  const __nv_bfloat16* kb = k + (size_t)bh * T * d + dd;
+  float acc = 0.f;
+  for (int i = lo; i < hi; ++i) {
+    if (cmp_block_of(i, T, n_cmp, l_prime, n_blk) != nb) continue;
+    const int r0 = i * cmp_stride;
+    float w = 0.f;
+    for (int j = 0; j < cmp_block; ++j) w += __bfloat162float(kb[(size_t)(r0 + j) * d]);
+    acc += w;
+  }
+  kblk[((size_t)bh * n_blk + nb) * d + dd] = acc * scale;
+}
+
+// Sort one (value, index) pair per lane across the warp, descending by value (ties: smaller
+// index first).
+__device__ __forceinline__ bool ranks_before(float a, int ai, float b, int bi) {
+  return a > b || (a == b && ai < bi);
+}
+__device__ __forceinline__ void bitonic_sort32_desc(float& v, int& ix, int lane) {
+#pragma unroll
+  for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, v, j);
+      const int oi = __shfl_xor_sync(0xffffffffu, ix, j);
+      const bool desc = (lane & k) == 0;   // this run sorts descending (k = 32: the whole warp)
+      const bool lower = (lane & j) == 0;  // lower lane of the pair keeps the better entry
+      const bool other_better = ranks_before(ov, oi, v, ix);
+      if ((lower == desc) ? other_better : !other_better && !(ov == v && oi == ix)) {
+        v = ov;
+        ix = oi;
+      }
+    }
+  }
+}
+// Merge a descending list (lv, li) with descending candidates (cv, ci): afterwards the list
+// holds the best 32 of both, descending.
+__device__ __forceinline__ void merge_top32(float& lv, int& li, float cv, int ci, int lane) {
+  const float rv = __shfl_sync(0xffffffffu, cv, 31 - lane);  // candidates reversed: ascending
+  const int ri = __shfl_sync(0xffffffffu, ci, 31 - lane);
+  if (ranks_before(rv, ri, lv, li)) {
+    lv = rv;
+    li = ri;
+  }
+  // (lv, li) is now bitonic and holds the best 32: one descending bitonic merge
+#pragma unroll
+  for (int j = 16; j > 0; j >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, lv, j);
+    const int oi = __shfl_xor_sync(0xffffffffu, li, j);
+    const bool lower = (lane & j) == 0;
+    const bool other_better = ranks_before(ov, oi, lv, li);
+    if (lower ? other_better : (!other_better && !(ov == lv && oi == li))) {
+      lv = ov;
+      li = oi;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads)
+    select_kernel(const __nv_bfloat16* __restrict__ q, const float* __restrict__ kblk, int32_t* __restrict__ sel,
+                  int Hq, int Hkv, int T, int d, int n_blk, int l_prime, int topk) {
+  extern __shared__ __align__(16) float sm[];
+  const int dp = d + 4;                      // padded row (floats)
+  float* qg = sm;                            // [kTile][dp]
+  float* kb = qg + kTile * dp;               // [kChunk][dp]
+  float* sc = kb + kChunk * dp;              // [kTile][kChunk + 1]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int bh = blockIdx.y, b = bh / Hkv, kvh = bh - (bh / Hkv) * Hkv;
+  const int G = Hq / Hkv;
+  const int t0 = blockIdx.x * kTile;
+
+  // group-summed queries of the tile (fp32), zero past the sequence end
+  for (int idx = tid; idx < kTile * d; idx += kThreads) {
+    const int tt = idx / d, dd = idx - (idx / d) * d, t = t0 + tt;
+    float s = 0.f;
+    if (t < T) {
+      const __nv_bfloat16* qp = q + (((size_t)b * Hq + (size_t)kvh * G) * T + t) * d + dd;
+      for (int g = 0; g < G; ++g) s += __bfloat162float(qp[(size_t)g * T * d]);
+    }
+    qg[tt * dp + dd] = s;
+  }
+
+  float lv[8];
+  int li[8];
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    lv[r] = -INFINITY;
+    li[r] = -1;
+  }
+  const int t_last = min(t0 + kTile, T) - 1;
+  const int nb_end = min(n_blk, t_last / l_prime + 1);  // blocks any token of the tile may see
+  const int ty = tid >> 4, tx = tid & 15;                // 4 tokens ty*4.., 4 blocks tx+16*j
+  const float* kblk_bh = kblk + (size_t)bh * n_blk * d;
+
+  for (int nb0 = 0; nb0 < nb_end; nb0 += kChunk) {
+    __syncthreads();  // qg written / previous chunk's kb and sc consumed
+    for (int idx = tid; idx < kChunk * (d / 4); idx += kThreads) {
+      const int r = idx / (d / 4), c4 = idx - r * (d / 4);
+      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (nb0 + r < n_blk) x = *reinterpret_cast<const float4*>(kblk_bh + (size_t)(nb0 + r) * d + 4 * c4);
+      *reinterpret_cast<float4*>(kb + r * dp + 4 * c4) = x;
+    }
+    __syncthreads();
+    float acc[4][4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[a][c] = 0.f;
+    for (int dd = 0; dd < d; dd += 4) {
+      float4 qa[4], ka[4];
+#pragma unroll
+      for (int a = 0; a < 4; ++a) qa[a] = *reinterpret_cast<const float4*>(qg + (ty * 4 + a) * dp + dd);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) ka[c] = *reinterpret_cast<const float4*>(kb + (tx + 16 * c) * dp + dd);
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          acc[a][c] = fmaf(qa[a].x, ka[c].x, acc[a][c]);
+          acc[a][c] = fmaf(qa[a].y, ka[c].y, acc[a][c]);
+          acc[a][c] = fmaf(qa[a].z, ka[c].z, acc[a][c]);
+          acc[a][c] = fmaf(qa[a].w, ka[c].w, acc[a][c]);
+        }
+    }
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+      const int tt = ty * 4 + a, t = t0 + tt;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int nb = nb0 + tx + 16 * c;
+        const bool vis = t < T && nb < n_blk && nb * l_prime <= t;
+        sc[tt * (kChunk + 1) + tx + 16 * c] = vis ? acc[a][c] : -INFINITY;
+      }
+    }
+    __syncthreads();
+    // merge this chunk into the running top-32 of the warp's 8 tokens (tokens warp + 8 r)
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const int tt = warp + 8 * r;
+      const float thr = __shfl_sync(0xffffffffu, lv[r], topk - 1);
+      const int thr_i = __shfl_sync(0xffffffffu, li[r], topk - 1);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float cv = sc[tt * (kChunk + 1) + lane + 32 * h];
+        int ci = nb0 + lane + 32 * h;
+        if (!__any_sync(0xffffffffu, ranks_before(cv, ci, thr, thr_i))) continue;
+        bitonic_sort32_desc(cv, ci, lane);
+        merge_top32(lv[r], li[r], cv, ci, lane);
+      }
+    }
+  }
+  // write the top-k of each token, -1 for entries that are not visible blocks
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    const int t = t0 + warp + 8 * r;
+    if (t < T && lane < topk)
+      sel[((size_t)bh * T + t) * topk + lane] = (lv[r] == -INFINITY) ? -1 : li[r];
+  }
+}
+
+}  // namespace select
+}  // namespace nsa

@@ -13,7 +13,9 @@ results:
   ``linspace(0, S-1, n_cmp)[i] <= t`` in float32 (nsa_reference.py:62-64);
 * block scores: group-summed queries against the compressed keys, summed into the selection
   block of each compressed key's linspace position, future blocks masked, top-n
-  (nsa_reference.py:27-44, 70-71);
+  (nsa_reference.py:27-44, 70-71) -- on the GPU by the selection kernel (``ops.select_blocks``);
+  ``block_scores``/``select_blocks`` below restate it with tensor ops (used on CPU and as a
+  cross-check);
 * sliding window: key s visible to query t iff ``0 <= t - s < window`` (nsa_reference.py:80-82);
 * gate: 1/3 each, or ``sigmoid(gate_w)`` normalised (nsa_reference.py:84-89);
 * fully masked rows give 0 (nsa_reference.py:24).
@@ -149,8 +151,9 @@ def nsa_forward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, *, n_sel: int
     o_cmp = compressed_branch(Q, Kc, Vc)
     if sel_override is not None:
         sel = sel_override.to(device=Q.device, dtype=torch.int32).contiguous()
-    else:
-        sel = select_blocks(Q, Kc, n_sel, l_prime)
+    else:  # the B200 selection kernel (scores in fp32, top-k per token)
+        sel = ops.select_blocks(Q.to(torch.bfloat16).contiguous(), K.to(torch.bfloat16).contiguous(), n_sel, l_prime,
+                                cmp_block, cmp_stride)
     o_sel = ops.forward(Q.to(torch.bfloat16).contiguous(), K.to(torch.bfloat16).contiguous(),
                         V.to(torch.bfloat16).contiguous(), sel, l_prime, 1)
     o_win = window_branch(Q, K, V, window)

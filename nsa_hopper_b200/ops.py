@@ -34,5 +34,12 @@ def forward_lse(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, sel: torch.Te
     return o, lse
 
 
+def select_blocks(Q: torch.Tensor, K: torch.Tensor, n_sel: int, l_prime: int = 64, cmp_block: int = 32,
+                  cmp_stride: int = 16) -> torch.Tensor:
+    """Block selection on the GPU (nsa_sel_select): int32 [B, Hkv, T, min(n_sel, ceil(T/l_prime))],
+    best block first, -1 where fewer blocks are visible (reference nsa_reference.py:27-44)."""
+    return _C.select_blocks(Q, K, int(n_sel), int(l_prime), int(cmp_block), int(cmp_stride))
+
+
 def library_version() -> int:
     return int(_C.library_version())

@@ -87,3 +87,28 @@ def test_validation_errors(kw, code):
 def test_shard_plan_counts_units():
     p = capi.plan(_desc(bkv_begin=1, bkv_end=3, qb_begin=100, qb_end=1100))
     assert p["n_units"] == 2 * 1000
+
+
+@pytest.mark.parametrize("args,code", [
+    (dict(q=0), capi.NSA_ERR_INVALID_ARG),
+    (dict(workspace=264), capi.NSA_ERR_INVALID_ARG),          # workspace must be 16-byte aligned
+    (dict(Hq=7), capi.NSA_ERR_INVALID_ARG),                   # Hq % Hkv != 0
+    (dict(d=66), capi.NSA_ERR_UNSUPPORTED),                   # d % 4 != 0
+    (dict(d=512), capi.NSA_ERR_UNSUPPORTED),                  # d > 256
+    (dict(n_sel=40), capi.NSA_ERR_UNSUPPORTED),               # top-k > 32
+    (dict(l_prime=0), capi.NSA_ERR_INVALID_ARG),
+])
+def test_select_validation_errors(args, code):
+    a = dict(q=256, k=256, workspace=256, sel=256, B=1, Hq=8, Hkv=2, T=4096, d=128, l_prime=64, n_sel=16)
+    a.update(args)
+    lib = capi.load()
+    rc = lib.nsa_sel_select(ctypes.c_void_p(a["q"]), ctypes.c_void_p(a["k"]), ctypes.c_void_p(a["workspace"]),
+                            ctypes.c_void_p(a["sel"]), a["B"], a["Hq"], a["Hkv"], a["T"], a["d"], a["l_prime"],
+                            a["n_sel"], 32, 16, None)
+    assert rc == code, capi.last_error()
+
+
+def test_select_workspace_bytes():
+    assert capi.select_workspace_bytes(1, 4, 65536, 128, 64) == 4 * 1024 * 128 * 4
+    assert capi.select_workspace_bytes(2, 2, 500, 64, 64) == 2 * 2 * 8 * 64 * 4
+    assert capi.select_workspace_bytes(0, 2, 500, 64, 64) == -1

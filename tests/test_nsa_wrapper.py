@@ -82,3 +82,48 @@ def test_nsa_forward_refuses_cpu_tensors():
     q = torch.zeros(1, 2, 64, 64)
     with pytest.raises(RuntimeError):
         nsa.nsa_forward(q, q[:, :1], q[:, :1])
+
+
+def _linspace_f32_device_rule(T, n):
+    """The selection kernel's float32 linspace (nsa_select_kernel.cuh: linspace_f32): step rounded
+    to float32, each value formed in double from the nearer end, then rounded."""
+    f32 = np.float32
+    if n == 1:
+        return np.zeros(1, f32)
+    step = f32(f32(T - 1) / f32(n - 1))
+    i = np.arange(n)
+    lo = (np.float64(step) * i).astype(f32)
+    hi = (np.float64(T - 1) - np.float64(step) * (n - 1 - i)).astype(f32)
+    return np.where(i < n // 2, lo, hi)
+
+
+def _floor_div_f32_device_rule(a, b):
+    f32 = np.float32
+    out = []
+    for x in a:
+        x, bb = f32(x), f32(b)
+        mod = f32(np.fmod(x, bb))
+        div = f32(f32(x - mod) / bb)
+        if mod != 0 and ((bb < 0) != (mod < 0)):
+            div = f32(div - f32(1))
+        if div != 0:
+            fl = f32(np.floor(div))
+            if f32(div - fl) > f32(0.5):
+                fl = f32(fl + f32(1))
+            out.append(fl)
+        else:
+            out.append(f32(np.copysign(f32(0), f32(x / bb))))
+    return np.array(out, dtype=f32)
+
+
+@pytest.mark.parametrize("T", [33, 100, 500, 512, 768, 1000, 1024, 2048, 4097, 8192, 12345, 65536, 131072])
+def test_selection_kernel_block_mapping_matches_reference(T):
+    """The compressed-key -> selection-block map the selection kernel derives on the device is the
+    reference's (src // l_prime) on torch.linspace (nsa_reference.py:35-36), bit for bit."""
+    n = (T - 32) // 16 + 1
+    ref = torch.linspace(0, T - 1, n).numpy()
+    mine = _linspace_f32_device_rule(T, n)
+    assert (ref.view(np.int32) == mine.view(np.int32)).all()
+    for lp in (64, 128, 256):
+        want = (torch.from_numpy(ref) // lp).numpy()
+        assert (_floor_div_f32_device_rule(mine, lp) == want).all()
