@@ -340,6 +340,69 @@ def run_ours(args, rank, world, local_rank):
     return result
 
 
+FP32_FMA_PEAK_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12  # nominal: 148 SMs x 128 FP32 lanes x FMA at max clock
+
+
+def run_select(args):
+    """--stage select: the block-selection kernel (nsa_sel_select) on the workload's shapes.
+    Algorithmic work per (b, kvh, token t): the group sum of G query rows (G*d adds) and one
+    d-long fp32 dot product per visible block (t // l_prime + 1 of them); bytes: Q (bf16) in,
+    k int32 indices out.  The scores run on the fp32 CUDA cores, so the roofline is the nominal
+    fp32 FMA peak (no measured figure exists for it on this pool)."""
+    import numpy as np
+    import torch
+
+    from nsa_hopper_b200 import capi, workload
+
+    w = workload.CONFIGS[args.config]
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    B, T, Hq, Hkv, D, lp, n = w.B, w.T, w.Hq, w.Hkv, w.d_qk, w.block, w.n
+    G = Hq // Hkv
+    gen = torch.Generator(device=dev).manual_seed(args.seed)
+    q = torch.randn(B, Hq, T, D, device=dev, generator=gen).to(torch.bfloat16)
+    k = torch.randn(B, Hkv, T, D, device=dev, generator=gen).to(torch.bfloat16)
+    n_blk = (T + lp - 1) // lp
+    kk = min(n, n_blk)
+    ws = torch.empty(capi.select_workspace_bytes(B, Hkv, T, D, lp) // 4, device=dev, dtype=torch.float32)
+    sel = torch.empty(B, Hkv, T, kk, device=dev, dtype=torch.int32)
+    flush = torch.empty(FLUSH_BYTES // 4, device=dev, dtype=torch.float32)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        capi.select(q.data_ptr(), k.data_ptr(), ws.data_ptr(), sel.data_ptr(), B, Hq, Hkv, T, D, lp, n, 32, 16,
+                    stream.cuda_stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    with ClockSampler(0) as clk:
+        for i in range(args.steps):
+            flush.fill_(float(i))
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+        torch.cuda.synchronize()
+    ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
+    t = np.arange(T, dtype=np.float64)
+    flops = B * Hkv * float(((t // lp + 1) * 2 * D).sum() + T * G * D)
+    byts = B * Hkv * T * (G * D * 2 + kk * 4)
+    achieved = flops / (ms * 1e-3) / 1e12
+    return {
+        "metric": "block selection (scores + top-k) tokens/s", "value": B * T / (ms * 1e-3), "unit": "tokens/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (bf16 inputs)", "data": "synthetic N(0,1) bf16 Q/K",
+        "config": {"workload": args.config, "stage": "select", "B": B, "T": T, "Hq": Hq, "Hkv": Hkv, "d": D,
+                   "block": lp, "top_n": n, "l2": "256 MiB buffer written between timed steps (L2 flushed)"},
+        "roofline": {"bound": "fp32", "achieved": achieved, "peak": FP32_FMA_PEAK_TFLOPS, "unit": "TFLOP/s",
+                     "frac": achieved / FP32_FMA_PEAK_TFLOPS, "traffic": None, "peak_kind": "nominal",
+                     "algorithmic_bytes_per_launch": byts, "hbm_gbs": byts / (ms * 1e-3) / 1e9},
+        "e2e": None, "clocks": clk.summary(), "gpu_launches": 2 * args.steps, "cpu_baseline": None,
+    }
+
+
 def cpu_baseline(args, seconds: float = 12.0):
     """Oracle (fp32, all host threads) on a bounded sample of the same workload: the last
     tokens of the sequence (full top-n cost), all KV heads.  Returns a dict."""
@@ -411,12 +474,19 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gather", action="store_true", help="skip the separately timed all-gather (N > 1)")
+    ap.add_argument("--stage", choices=["selected", "select"], default="selected",
+                    help="selected: the selected-branch forward (the headline); select: the block-selection kernel")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
     world = _env_int("WORLD_SIZE", 1)
     rank = _env_int("RANK", 0)
     local_rank = _env_int("LOCAL_RANK", 0)
+
+    if args.stage == "select":
+        if rank == 0:
+            print(json.dumps(run_select(args)), flush=True)
+        return
 
     if args.impl == "reference":
         res = run_reference(args, rank, world)
