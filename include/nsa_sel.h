@@ -9,7 +9,8 @@
  *
  * (reference nsa_v0.cu:118-146, nsa_v1.cu:125-147, nsa_v2.cu:147-170).  Every entry point
  * takes plain pointers and sizes; no torch type crosses this boundary.  The library never
- * allocates device memory: all buffers belong to the caller.  All launches go to the stream
+ * calls cudaMalloc: all buffers belong to the caller, except one static device array inside the
+ * library (16 MB) that only nsa_sel_select_noalloc uses.  All launches go to the stream
  * passed in; a call returns as soon as the work is queued (like the reference op, which is
  * asynchronous on the legacy stream).  The library is reentrant: concurrent calls from
  * several host threads are safe; the error text is kept per host thread.
@@ -147,6 +148,19 @@ int nsa_sel_select(const void* q, const void* k, float* kblk_workspace, int32_t*
 /* Bytes of the workspace nsa_sel_select needs (B * Hkv * ceil(T / l_prime) * d * 4), -1 if
    an argument is not positive. */
 int64_t nsa_sel_select_workspace_bytes(int32_t B, int32_t Hkv, int32_t T, int32_t d, int32_t l_prime);
+
+/* nsa_sel_select without a caller workspace and without any allocation: the block-key table is
+   kept in a static device array of nsa_sel_select_static_scratch_bytes() bytes inside the
+   library (its address is resolved once per device with cudaGetSymbolAddress; the library
+   never calls cudaMalloc).  Requests whose workspace would exceed it return
+   NSA_ERR_UNSUPPORTED without launching.  The scratch is shared per device: calls on one device
+   must not run concurrently on different streams. */
+int nsa_sel_select_noalloc(const void* q, const void* k, int32_t* sel_out, int32_t B, int32_t Hq, int32_t Hkv,
+                           int32_t T, int32_t d, int32_t l_prime, int32_t n_sel, int32_t cmp_block,
+                           int32_t cmp_stride, nsa_stream_t stream);
+
+/* Size in bytes of the static scratch used by nsa_sel_select_noalloc. */
+int64_t nsa_sel_select_static_scratch_bytes(void);
 
 /* Text of the last error on this host thread ("" if none). */
 const char* nsa_sel_last_error(void);

@@ -94,6 +94,10 @@ def load(path: Optional[str] = None) -> ctypes.CDLL:
     lib.nsa_sel_select.restype = ctypes.c_int
     lib.nsa_sel_select_workspace_bytes.argtypes = [i32] * 5
     lib.nsa_sel_select_workspace_bytes.restype = ctypes.c_int64
+    lib.nsa_sel_select_noalloc.argtypes = [vp, vp, vp] + [i32] * 9 + [vp]
+    lib.nsa_sel_select_noalloc.restype = ctypes.c_int
+    lib.nsa_sel_select_static_scratch_bytes.argtypes = []
+    lib.nsa_sel_select_static_scratch_bytes.restype = ctypes.c_int64
     if path is None:
         _lib = lib
     return lib
@@ -145,3 +149,10 @@ def select(q: int, k: int, workspace: int, sel_out: int, B: int, Hq: int, Hkv: i
     check(load().nsa_sel_select(ctypes.c_void_p(q), ctypes.c_void_p(k), ctypes.c_void_p(workspace),
                                 ctypes.c_void_p(sel_out), B, Hq, Hkv, T, d, l_prime, n_sel, cmp_block, cmp_stride,
                                 ctypes.c_void_p(stream)))
+
+
+def select_noalloc(q: int, k: int, sel_out: int, B: int, Hq: int, Hkv: int, T: int, d: int, l_prime: int,
+                   n_sel: int, cmp_block: int = 32, cmp_stride: int = 16, stream: int = 0) -> None:
+    """nsa_sel_select_noalloc: block selection with the library's static scratch (no allocation)."""
+    check(load().nsa_sel_select_noalloc(ctypes.c_void_p(q), ctypes.c_void_p(k), ctypes.c_void_p(sel_out), B, Hq,
+                                        Hkv, T, d, l_prime, n_sel, cmp_block, cmp_stride, ctypes.c_void_p(stream)))

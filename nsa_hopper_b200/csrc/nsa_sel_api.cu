@@ -393,7 +393,28 @@ int launch(const nsa_sel_desc* d, nsa_stream_t stream) {
 
 }  // namespace
 
+// Static scratch of the allocation-free selection entry point (nsa_sel_select_noalloc): the
+// block-key table lives in this module-scope device array, so the call never allocates.
+constexpr size_t kStaticSelectScratchFloats = (size_t)4 << 20;  // 16 MB
+__device__ __align__(256) float g_select_scratch[kStaticSelectScratchFloats];
+
 namespace {
+float* g_select_scratch_ptr[kMaxDevices] = {};
+
+// Resolve the static scratch's device address once per device (this also loads the module, so
+// no later call allocates).
+int static_select_scratch(int dev, float** out) {
+  std::lock_guard<std::mutex> lk(g_dev.mu);
+  if (g_select_scratch_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_select_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(select scratch)");
+    g_select_scratch_ptr[dev] = static_cast<float*>(ptr);
+  }
+  *out = g_select_scratch_ptr[dev];
+  return NSA_OK;
+}
+
 // ------------------------------------------------------------------ block selection
 int select_shape(int32_t B, int32_t Hq, int32_t Hkv, int32_t T, int32_t d, int32_t l_prime, int32_t n_sel,
                  int32_t cmp_block, int32_t cmp_stride, int* n_blk, int* topk, int* n_cmp) {
@@ -464,6 +485,27 @@ int nsa_sel_select(const void* q, const void* k, float* kblk_workspace, int32_t*
   g_last_error[0] = '\0';
   return NSA_OK;
 }
+
+int nsa_sel_select_noalloc(const void* q, const void* k, int32_t* sel_out, int32_t B, int32_t Hq, int32_t Hkv,
+                           int32_t T, int32_t d, int32_t l_prime, int32_t n_sel, int32_t cmp_block,
+                           int32_t cmp_stride, nsa_stream_t stream) {
+  int n_blk = 0, topk = 0, n_cmp = 0;
+  int rc = select_shape(B, Hq, Hkv, T, d, l_prime, n_sel, cmp_block, cmp_stride, &n_blk, &topk, &n_cmp);
+  if (rc != NSA_OK) return rc;
+  const int64_t need = nsa_sel_select_workspace_bytes(B, Hkv, T, d, l_prime);
+  if (need < 0 || (uint64_t)need > kStaticSelectScratchFloats * sizeof(float))
+    return fail(NSA_ERR_UNSUPPORTED, "selection needs %lld bytes of scratch; the static scratch holds %zu",
+                (long long)need, kStaticSelectScratchFloats * sizeof(float));
+  int sm = 0, dev = 0;
+  rc = current_sm_count(&sm, &dev);
+  if (rc != NSA_OK) return rc;
+  float* scratch = nullptr;
+  rc = static_select_scratch(dev, &scratch);
+  if (rc != NSA_OK) return rc;
+  return nsa_sel_select(q, k, scratch, sel_out, B, Hq, Hkv, T, d, l_prime, n_sel, cmp_block, cmp_stride, stream);
+}
+
+int64_t nsa_sel_select_static_scratch_bytes(void) { return (int64_t)(kStaticSelectScratchFloats * sizeof(float)); }
 
 int nsa_sel_run(const nsa_sel_desc* desc, nsa_stream_t stream) { return launch(desc, stream); }
 
