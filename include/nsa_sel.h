@@ -139,7 +139,7 @@ int nsa_sel_plan(const nsa_sel_desc* desc, int32_t sm_count, nsa_sel_plan_info* 
    the k best visible blocks (nb * l_prime <= t) by score, highest first; -1 where fewer than k
    blocks are visible (the reference's topk returns masked future blocks there, which the
    selected branch ignores in the same way).  Scores are fp32.  q, k bf16 as in nsa_sel_forward
-   (d_qk = d); kblk_workspace: caller-owned fp32 buffer of nsa_sel_select_workspace_bytes()
+   (d_qk = d, d % 8 == 0, d <= 256; q 16-byte aligned); kblk_workspace: caller-owned fp32 buffer of nsa_sel_select_workspace_bytes()
    bytes, 16-byte aligned.  Two kernel launches on `stream`. */
 int nsa_sel_select(const void* q, const void* k, float* kblk_workspace, int32_t* sel_out, int32_t B, int32_t Hq,
                    int32_t Hkv, int32_t T, int32_t d, int32_t l_prime, int32_t n_sel, int32_t cmp_block,

@@ -422,7 +422,8 @@ int select_shape(int32_t B, int32_t Hq, int32_t Hkv, int32_t T, int32_t d, int32
       cmp_stride <= 0)
     return fail(NSA_ERR_INVALID_ARG, "B, Hq, Hkv, T, d, l_prime, n_sel, cmp_block and cmp_stride must be positive");
   if (Hq % Hkv != 0) return fail(NSA_ERR_INVALID_ARG, "Hq (%d) must be a multiple of Hkv (%d)", Hq, Hkv);
-  if (d % 4 != 0 || d > nsa::select::kMaxD) return fail(NSA_ERR_UNSUPPORTED, "d=%d: selection supports d % 4 == 0, d <= %d", d, nsa::select::kMaxD);
+  if (d % 8 != 0 || d > nsa::select::kMaxD)
+    return fail(NSA_ERR_UNSUPPORTED, "d=%d: selection supports d %% 8 == 0, d <= %d", d, nsa::select::kMaxD);
   if ((long long)B * Hkv > 65535) return fail(NSA_ERR_UNSUPPORTED, "B*Hkv exceeds 65535");
   if ((long long)B * Hq * T * d >= (1ll << 40)) return fail(NSA_ERR_UNSUPPORTED, "problem too large");
   *n_blk = (T + l_prime - 1) / l_prime;
@@ -449,9 +450,9 @@ int nsa_sel_select(const void* q, const void* k, float* kblk_workspace, int32_t*
     return fail(NSA_ERR_INVALID_ARG, "q, k, kblk_workspace and sel_out must be non-NULL");
   if ((reinterpret_cast<uintptr_t>(kblk_workspace) & 15u) != 0)
     return fail(NSA_ERR_INVALID_ARG, "kblk_workspace must be 16-byte aligned");
-  if ((reinterpret_cast<uintptr_t>(q) & 1u) != 0 || (reinterpret_cast<uintptr_t>(k) & 1u) != 0 ||
+  if ((reinterpret_cast<uintptr_t>(q) & 15u) != 0 || (reinterpret_cast<uintptr_t>(k) & 1u) != 0 ||
       (reinterpret_cast<uintptr_t>(sel_out) & 3u) != 0)
-    return fail(NSA_ERR_INVALID_ARG, "q, k and sel_out must be aligned to their element size");
+    return fail(NSA_ERR_INVALID_ARG, "q must be 16-byte aligned, k and sel_out aligned to their element size");
   int n_blk = 0, topk = 0, n_cmp = 0;
   int rc = select_shape(B, Hq, Hkv, T, d, l_prime, n_sel, cmp_block, cmp_stride, &n_blk, &topk, &n_cmp);
   if (rc != NSA_OK) return rc;

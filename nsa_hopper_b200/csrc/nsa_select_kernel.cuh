@@ -16,9 +16,10 @@
 //    tile (fp32) stays in shared memory; block-key tiles of 64 blocks stream through shared
 //    memory; each thread computes a 4 x 4 register tile of scores (fp32 FMA: the ranking must
 //    agree with the reference's fp64 one except at near-ties, which bf16 or tf32 tensor-core
-//    products would not).  Each warp keeps, for 8 tokens, the running top-32 (score, block) in
-//    registers, one entry per lane, sorted by a warp-wide bitonic network; a chunk of
-//    candidates is merged only if one of them beats the current k-th score.
+//    products would not).  Each warp keeps, for 8 tokens, the running top-k (score, block) in
+//    registers, one entry per lane, in descending order; a candidate that beats the current
+//    k-th entry is inserted at its rank (ballot + popcount) while the entries below it shift
+//    down one lane, so after the first chunks only the few improving candidates cost work.
 #pragma once
 #include <cuda_bf16.h>
 #include <stdint.h>
@@ -86,48 +87,22 @@ __global__ void kblk_kernel(const __nv_bfloat16* __restrict__ k, float* __restri
   kblk[((size_t)bh * n_blk + nb) * d + dd] = acc * scale;
 }
 
-// Sort one (value, index) pair per lane across the warp, descending by value (ties: smaller
-// index first).
+// Ranking of (score, block) pairs: higher score first, ties by smaller block index.
 __device__ __forceinline__ bool ranks_before(float a, int ai, float b, int bi) {
   return a > b || (a == b && ai < bi);
 }
-__device__ __forceinline__ void bitonic_sort32_desc(float& v, int& ix, int lane) {
-#pragma unroll
-  for (int k = 2; k <= 32; k <<= 1) {
-#pragma unroll
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, v, j);
-      const int oi = __shfl_xor_sync(0xffffffffu, ix, j);
-      const bool desc = (lane & k) == 0;   // this run sorts descending (k = 32: the whole warp)
-      const bool lower = (lane & j) == 0;  // lower lane of the pair keeps the better entry
-      const bool other_better = ranks_before(ov, oi, v, ix);
-      if ((lower == desc) ? other_better : !other_better && !(ov == v && oi == ix)) {
-        v = ov;
-        ix = oi;
-      }
-    }
-  }
-}
-// Merge a descending list (lv, li) with descending candidates (cv, ci): afterwards the list
-// holds the best 32 of both, descending.
-__device__ __forceinline__ void merge_top32(float& lv, int& li, float cv, int ci, int lane) {
-  const float rv = __shfl_sync(0xffffffffu, cv, 31 - lane);  // candidates reversed: ascending
-  const int ri = __shfl_sync(0xffffffffu, ci, 31 - lane);
-  if (ranks_before(rv, ri, lv, li)) {
-    lv = rv;
-    li = ri;
-  }
-  // (lv, li) is now bitonic and holds the best 32: one descending bitonic merge
-#pragma unroll
-  for (int j = 16; j > 0; j >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, lv, j);
-    const int oi = __shfl_xor_sync(0xffffffffu, li, j);
-    const bool lower = (lane & j) == 0;
-    const bool other_better = ranks_before(ov, oi, lv, li);
-    if (lower ? other_better : (!other_better && !(ov == lv && oi == li))) {
-      lv = ov;
-      li = oi;
-    }
+// Insert (v, vi) into a descending list held one entry per lane: entries ranked before it stay,
+// the rest move down one lane (the last one drops out).
+__device__ __forceinline__ void insert_sorted(float& lv, int& li, float v, int vi, int lane) {
+  const int pos = __popc(__ballot_sync(0xffffffffu, ranks_before(lv, li, v, vi)));
+  const float up = __shfl_up_sync(0xffffffffu, lv, 1);
+  const int upi = __shfl_up_sync(0xffffffffu, li, 1);
+  if (lane == pos) {
+    lv = v;
+    li = vi;
+  } else if (lane > pos) {
+    lv = up;
+    li = upi;
   }
 }
 
@@ -144,15 +119,29 @@ __global__ void __launch_bounds__(kThreads)
   const int G = Hq / Hkv;
   const int t0 = blockIdx.x * kTile;
 
-  // group-summed queries of the tile (fp32), zero past the sequence end
-  for (int idx = tid; idx < kTile * d; idx += kThreads) {
-    const int tt = idx / d, dd = idx - (idx / d) * d, t = t0 + tt;
-    float s = 0.f;
+  // group-summed queries of the tile (fp32), zero past the sequence end; 8 dimensions per item
+  // (one 16-byte load per head)
+  const int d8 = d / 8;
+  for (int idx = tid; idx < kTile * d8; idx += kThreads) {
+    const int tt = idx / d8, c8 = idx - (idx / d8) * d8, t = t0 + tt;
+    float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     if (t < T) {
-      const __nv_bfloat16* qp = q + (((size_t)b * Hq + (size_t)kvh * G) * T + t) * d + dd;
-      for (int g = 0; g < G; ++g) s += __bfloat162float(qp[(size_t)g * T * d]);
+      const uint4* qp = reinterpret_cast<const uint4*>(q + (((size_t)b * Hq + (size_t)kvh * G) * T + t) * d) + c8;
+      const size_t head_stride = (size_t)T * d / 8;
+      for (int g = 0; g < G; ++g) {
+        const uint4 v = __ldg(qp + (size_t)g * head_stride);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(h[e]);
+          s[2 * e] += f.x;
+          s[2 * e + 1] += f.y;
+        }
+      }
     }
-    qg[tt * dp + dd] = s;
+    float* dst = qg + tt * dp + 8 * c8;
+    *reinterpret_cast<float4*>(dst) = make_float4(s[0], s[1], s[2], s[3]);
+    *reinterpret_cast<float4*>(dst + 4) = make_float4(s[4], s[5], s[6], s[7]);
   }
 
   float lv[8];
@@ -208,19 +197,28 @@ __global__ void __launch_bounds__(kThreads)
       }
     }
     __syncthreads();
-    // merge this chunk into the running top-32 of the warp's 8 tokens (tokens warp + 8 r)
+    // insert this chunk's candidates into the running top-k of the warp's 8 tokens (tokens
+    // warp + 8 r): only candidates that beat the current k-th entry are inserted, one at a time
 #pragma unroll
     for (int r = 0; r < 8; ++r) {
       const int tt = warp + 8 * r;
-      const float thr = __shfl_sync(0xffffffffu, lv[r], topk - 1);
-      const int thr_i = __shfl_sync(0xffffffffu, li[r], topk - 1);
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        float cv = sc[tt * (kChunk + 1) + lane + 32 * h];
-        int ci = nb0 + lane + 32 * h;
-        if (!__any_sync(0xffffffffu, ranks_before(cv, ci, thr, thr_i))) continue;
-        bitonic_sort32_desc(cv, ci, lane);
-        merge_top32(lv[r], li[r], cv, ci, lane);
+        const float cv = sc[tt * (kChunk + 1) + lane + 32 * h];
+        const int ci = nb0 + lane + 32 * h;
+        float thr = __shfl_sync(0xffffffffu, lv[r], topk - 1);
+        int thr_i = __shfl_sync(0xffffffffu, li[r], topk - 1);
+        unsigned m = __ballot_sync(0xffffffffu, ranks_before(cv, ci, thr, thr_i));
+        while (m != 0u) {
+          const int src = __ffs(m) - 1;
+          m &= m - 1u;
+          const float v = __shfl_sync(0xffffffffu, cv, src);
+          const int vi = __shfl_sync(0xffffffffu, ci, src);
+          if (!ranks_before(v, vi, thr, thr_i)) continue;  // the k-th entry rose past it meanwhile
+          insert_sorted(lv[r], li[r], v, vi, lane);
+          thr = __shfl_sync(0xffffffffu, lv[r], topk - 1);
+          thr_i = __shfl_sync(0xffffffffu, li[r], topk - 1);
+        }
       }
     }
   }

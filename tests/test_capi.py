@@ -93,7 +93,8 @@ def test_shard_plan_counts_units():
     (dict(q=0), capi.NSA_ERR_INVALID_ARG),
     (dict(workspace=264), capi.NSA_ERR_INVALID_ARG),          # workspace must be 16-byte aligned
     (dict(Hq=7), capi.NSA_ERR_INVALID_ARG),                   # Hq % Hkv != 0
-    (dict(d=66), capi.NSA_ERR_UNSUPPORTED),                   # d % 4 != 0
+    (dict(d=68), capi.NSA_ERR_UNSUPPORTED),                   # d % 8 != 0
+    (dict(q=258), capi.NSA_ERR_INVALID_ARG),                  # q must be 16-byte aligned
     (dict(d=512), capi.NSA_ERR_UNSUPPORTED),                  # d > 256
     (dict(n_sel=40), capi.NSA_ERR_UNSUPPORTED),               # top-k > 32
     (dict(l_prime=0), capi.NSA_ERR_INVALID_ARG),
