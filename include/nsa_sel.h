@@ -62,6 +62,9 @@ typedef struct CUstream_st* nsa_stream_t;
 #define NSA_DTYPE_BF16 0
 #define NSA_DTYPE_F32 1
 
+#define NSA_KEYMAP_CAUSAL 0     /* key position p is visible to query t iff p <= t */
+#define NSA_KEYMAP_COMPRESSED 1 /* compressed key i is visible iff linspace(0, T-1, kv_len)[i] <= t */
+
 /* Full description of one call.  Zero-initialise, then fill the fields you need. */
 typedef struct nsa_sel_desc {
   const void* q;              /* bf16 [B, Hq, T, d_qk] */
@@ -89,7 +92,16 @@ typedef struct nsa_sel_desc {
   int32_t timeout_ms;         /* bound on every in-kernel wait; 0 = default (2000 ms) */
   int32_t max_ctas;           /* 0 = one CTA per SM */
   int32_t debug_flags;        /* NSA_DEBUG_* bits; 0 in normal use */
-  int32_t reserved[5];
+  /* Key visibility beyond the causal default (the sliding-window and compressed branches of NSA,
+     reference nsa_reference.py:59-64 and 79-82, run on the same kernel): */
+  int32_t kv_len;             /* K/V rows per (b, kvh); 0 = seq_len.  Other values need
+                                 key_map = NSA_KEYMAP_COMPRESSED (then K, V are [B, Hkv, kv_len, d]) */
+  int32_t window;             /* > 0: key p is visible to query t only if t - p < window (causal
+                                 key map only; not with cu_seqlens) */
+  int32_t key_map;            /* NSA_KEYMAP_CAUSAL: key p visible to query t iff p <= t;
+                                 NSA_KEYMAP_COMPRESSED: key i visible iff the float32
+                                 linspace(0, seq_len-1, kv_len)[i] <= t (not with cu_seqlens) */
+  int32_t reserved[2];
 } nsa_sel_desc;
 
 /* Launch plan chosen for a description (filled by nsa_sel_plan, used by the launcher). */

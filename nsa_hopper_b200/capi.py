@@ -27,6 +27,8 @@ NSA_DEVERR_TIMEOUT = 1
 NSA_DEBUG_STALL = 1
 DTYPE_BF16 = 0
 DTYPE_F32 = 1
+KEYMAP_CAUSAL = 0
+KEYMAP_COMPRESSED = 1
 
 
 class NsaSelDesc(ctypes.Structure):
@@ -44,7 +46,10 @@ class NsaSelDesc(ctypes.Structure):
         ("bkv_begin", ctypes.c_int32), ("bkv_end", ctypes.c_int32),
         ("qb_begin", ctypes.c_int32), ("qb_end", ctypes.c_int32),
         ("timeout_ms", ctypes.c_int32), ("max_ctas", ctypes.c_int32), ("debug_flags", ctypes.c_int32),
-        ("reserved", ctypes.c_int32 * 5),
+        ("kv_len", ctypes.c_int32),
+        ("window", ctypes.c_int32),
+        ("key_map", ctypes.c_int32),
+        ("reserved", ctypes.c_int32 * 2),
     ]
 
 

@@ -96,20 +96,21 @@ typedef void (*KernelFn)(const CUtensorMap, const CUtensorMap, const CUtensorMap
 typedef nsa::SmemLayout (*LayoutFn)(int, int, int, int);
 
 struct Variant {
-  int dqk, dv, ncol, out_f32, nwg, vgroups, threads;
+  int dqk, dv, ncol, out_f32, nwg, ext, vgroups, threads;
   KernelFn kernel;
   LayoutFn layout;
   int k_stage, v_stage, tmem_cols;
 };
 
-template <int DQK, int DV, int NCOL, typename OutT, int NWG>
+template <int DQK, int DV, int NCOL, typename OutT, int NWG, bool EXT = false>
 Variant make_variant() {
-  using C = nsa::Cfg<DQK, DV, NCOL, OutT, NWG>;
+  using C = nsa::Cfg<DQK, DV, NCOL, OutT, NWG, EXT>;
   return Variant{DQK,
                  DV,
                  NCOL,
                  sizeof(OutT) == 4 ? 1 : 0,
                  NWG,
+                 EXT ? 1 : 0,
                  C::kVGroups,
                  C::kThreads,
                  reinterpret_cast<KernelFn>(&nsa::nsa_sel_fwd_kernel<C>),
@@ -126,18 +127,25 @@ Variant make_variant() {
       make_variant<DQK, DV, 64, bf16, 1>(), make_variant<DQK, DV, 16, float, 2>(),                      \
       make_variant<DQK, DV, 32, float, 1>(), make_variant<DQK, DV, 64, float, 1>()
 
+// Extended key visibility (window, compressed key map): the NSA window and compressed branches,
+// fp32 output, d_qk == d_v in {64, 128}.
+#define NSA_EXT_VARIANTS_FOR(D)                                                                      \
+  make_variant<D, D, 16, float, 2, true>(), make_variant<D, D, 32, float, 1, true>(),                 \
+      make_variant<D, D, 64, float, 1, true>()
+
 const Variant* variants(int* n) {
-  static const Variant v[] = {NSA_VARIANTS_FOR(64, 64), NSA_VARIANTS_FOR(128, 128), NSA_VARIANTS_FOR(192, 128),
-                              NSA_VARIANTS_FOR(128, 64)};
+  static const Variant v[] = {NSA_VARIANTS_FOR(64, 64),  NSA_VARIANTS_FOR(128, 128), NSA_VARIANTS_FOR(192, 128),
+                              NSA_VARIANTS_FOR(128, 64), NSA_EXT_VARIANTS_FOR(64),   NSA_EXT_VARIANTS_FOR(128)};
   *n = (int)(sizeof(v) / sizeof(v[0]));
   return v;
 }
 
-int find_variant(int dqk, int dv, int ncol, int out_f32) {
+int find_variant(int dqk, int dv, int ncol, int out_f32, int ext) {
   int n = 0;
   const Variant* v = variants(&n);
   for (int i = 0; i < n; ++i)
-    if (v[i].dqk == dqk && v[i].dv == dv && v[i].ncol == ncol && v[i].out_f32 == out_f32) return i;
+    if (v[i].dqk == dqk && v[i].dv == dv && v[i].ncol == ncol && v[i].out_f32 == out_f32 && v[i].ext == ext)
+      return i;
   return -1;
 }
 
@@ -177,13 +185,25 @@ int make_plan(const nsa_sel_desc* d, int sm_count, Plan* pl) {
                 kMaxSub);
   if (d->o_dtype != NSA_DTYPE_BF16 && d->o_dtype != NSA_DTYPE_F32)
     return fail(NSA_ERR_INVALID_ARG, "o_dtype must be NSA_DTYPE_BF16 or NSA_DTYPE_F32");
+  const int kv_len = d->kv_len > 0 ? d->kv_len : T;
+  if (d->kv_len < 0) return fail(NSA_ERR_INVALID_ARG, "kv_len must be >= 0 (0 = seq_len)");
+  if (d->window < 0) return fail(NSA_ERR_INVALID_ARG, "window must be >= 0 (0 = none)");
+  if (d->key_map != NSA_KEYMAP_CAUSAL && d->key_map != NSA_KEYMAP_COMPRESSED)
+    return fail(NSA_ERR_INVALID_ARG, "key_map must be NSA_KEYMAP_CAUSAL or NSA_KEYMAP_COMPRESSED");
+  if (d->key_map == NSA_KEYMAP_CAUSAL && kv_len != T)
+    return fail(NSA_ERR_INVALID_ARG, "kv_len (%d) != seq_len (%d) needs key_map = NSA_KEYMAP_COMPRESSED", kv_len, T);
+  if (d->key_map == NSA_KEYMAP_COMPRESSED && d->window > 0)
+    return fail(NSA_ERR_UNSUPPORTED, "window and key_map = NSA_KEYMAP_COMPRESSED cannot be combined");
+  if (d->cu_seqlens != nullptr && (d->window > 0 || d->key_map != NSA_KEYMAP_CAUSAL))
+    return fail(NSA_ERR_UNSUPPORTED, "a varlen batch supports neither window nor key_map");
   if (d->cu_seqlens != nullptr) {
     if (B != 1) return fail(NSA_ERR_INVALID_ARG, "a varlen batch (cu_seqlens) needs B == 1");
     if (d->q_block != 1) return fail(NSA_ERR_UNSUPPORTED, "a varlen batch needs per-token selection (BQ == 1)");
     if (d->n_seqs <= 0) return fail(NSA_ERR_INVALID_ARG, "n_seqs must be positive with cu_seqlens");
   }
   // 32-bit coordinates and index arithmetic inside the kernel.
-  if ((long long)T * d->d_qk >= (1ll << 31) || (long long)B * Hkv * NQB * d->n_sel >= (1ll << 31))
+  if ((long long)kv_len * d->d_qk >= (1ll << 31) || (long long)T >= (1ll << 24) ||
+      (long long)T * d->d_qk >= (1ll << 31) || (long long)B * Hkv * NQB * d->n_sel >= (1ll << 31))
     return fail(NSA_ERR_UNSUPPORTED, "problem too large for 32-bit coordinates");
 
   // Tokens per work unit: the largest divisor of BQ with G * tokens <= 128.
@@ -193,10 +213,13 @@ int make_plan(const nsa_sel_desc* d, int sm_count, Plan* pl) {
   const int rows = G * bqs;
   int ncol = 16;
   while (ncol < rows) ncol <<= 1;
-  const int vi = find_variant(d->d_qk, d->d_v, ncol, d->o_dtype == NSA_DTYPE_F32 ? 1 : 0);
+  const int ext = (d->window > 0 || d->key_map != NSA_KEYMAP_CAUSAL) ? 1 : 0;
+  const int vi = find_variant(d->d_qk, d->d_v, ncol, d->o_dtype == NSA_DTYPE_F32 ? 1 : 0, ext);
   if (vi < 0)
-    return fail(NSA_ERR_UNSUPPORTED, "no kernel for (d_qk=%d, d_v=%d); built: (64,64), (128,128), (192,128), (128,64)",
-                d->d_qk, d->d_v);
+    return fail(NSA_ERR_UNSUPPORTED,
+                ext ? "no kernel with window / key map for (d_qk=%d, d_v=%d, %s O); built: d_qk == d_v in {64, 128}, fp32 O"
+                    : "no kernel for (d_qk=%d, d_v=%d, %s O); built: (64,64), (128,128), (192,128), (128,64)",
+                d->d_qk, d->d_v, d->o_dtype == NSA_DTYPE_F32 ? "fp32" : "bf16");
   int nv = 0;
   const Variant& V = variants(&nv)[vi];
 
@@ -283,6 +306,7 @@ int launch(const nsa_sel_desc* d, nsa_stream_t stream) {
 
   const int B = d->batch, Hq = d->heads_q, Hkv = d->heads_kv, T = d->seq_len;
   const cuuint64_t dqk = (cuuint64_t)d->d_qk, dv = (cuuint64_t)d->d_v;
+  const cuuint64_t KVL = (cuuint64_t)(d->kv_len > 0 ? d->kv_len : T);  // K/V rows per (b, kvh)
   CUtensorMap tmQ, tmK, tmV, tmO;
   {
     cuuint64_t dims[4] = {dqk, (cuuint64_t)T, (cuuint64_t)Hq, (cuuint64_t)B};
@@ -293,8 +317,8 @@ int launch(const nsa_sel_desc* d, nsa_stream_t stream) {
     if (rc != NSA_OK) return rc;
   }
   {
-    cuuint64_t dims[3] = {dqk, (cuuint64_t)T, (cuuint64_t)B * Hkv};
-    cuuint64_t str[2] = {dqk * 2, dqk * 2 * T};
+    cuuint64_t dims[3] = {dqk, KVL, (cuuint64_t)B * Hkv};
+    cuuint64_t str[2] = {dqk * 2, dqk * 2 * KVL};
     cuuint32_t box[3] = {64, 64, 1};
     rc = encode(&tmK, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, d->k, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B,
                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "K");
@@ -303,8 +327,8 @@ int launch(const nsa_sel_desc* d, nsa_stream_t stream) {
   {
     // V viewed as (64 d, T, d_v/64 slices, B*Hkv): one box = a 64-key sub-block, slice-major in
     // shared memory ([slice][row][64]), the MN-major layout the PV UMMA reads.
-    cuuint64_t dims[4] = {64, (cuuint64_t)T, dv / 64, (cuuint64_t)B * Hkv};
-    cuuint64_t str[3] = {dv * 2, 128, dv * 2 * T};
+    cuuint64_t dims[4] = {64, KVL, dv / 64, (cuuint64_t)B * Hkv};
+    cuuint64_t str[3] = {dv * 2, 128, dv * 2 * KVL};
     cuuint32_t box[4] = {64, 64, (cuuint32_t)(dv / 64), 1};
     rc = encode(&tmV, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, d->v, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B,
                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "V");
@@ -367,6 +391,9 @@ int launch(const nsa_sel_desc* d, nsa_stream_t stream) {
   p.off_ml = pl.layout.off_ml;
   p.off_info = pl.layout.off_info;
   p.off_bar = pl.layout.off_bar;
+  p.kv_len = (int)KVL;
+  p.window = d->window;
+  p.key_map = d->key_map;
   p.debug_stall = (d->debug_flags & NSA_DEBUG_STALL) ? 1 : 0;
   p.out_bufs = pl.out_bufs;
 

@@ -44,7 +44,9 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 #include <math.h>
+#include <limits.h>
 #include "ptx.cuh"
+#include "nsa_linspace.cuh"
 
 namespace nsa {
 
@@ -107,6 +109,10 @@ struct Params {
   float scale_log2;
   unsigned long long timeout_ns;
   uint32_t off_k, off_v, off_q, off_p, off_out, off_tr, off_alpha, off_fac, off_ml, off_info, off_bar;
+  // Key visibility: key position p (0..kv_len) is visible to query token t iff p <= hi(t) and
+  // p >= t - window + 1 (window > 0 only); hi(t) = t, or with key_map = 1 (compressed keys) the
+  // last key whose float32 linspace(0, T-1, kv_len) position is <= t.
+  int kv_len, window, key_map;
   int debug_stall;  // 1: the MMA warp first waits on a barrier nothing arrives on (error-path test)
   int out_bufs;     // output staging tiles (2: double buffer; 1 when shared memory is tight)
 };
@@ -143,9 +149,12 @@ __host__ __device__ constexpr int ceil_pow2_32(int x) {
 }
 __host__ __device__ constexpr uint32_t align_up(uint32_t x, uint32_t a) { return (x + a - 1) / a * a; }
 
-template <int DQK_, int DV_, int NCOL_, typename OutT_, int NWG_>
+// EXT_: key visibility beyond the causal default (window bound, compressed key map; the
+// Params fields window / key_map / kv_len).  The causal instantiations keep the plain mask.
+template <int DQK_, int DV_, int NCOL_, typename OutT_, int NWG_, bool EXT_ = false>
 struct Cfg {
   static constexpr int DQK = DQK_, DV = DV_, NCOL = NCOL_, NWG = NWG_;
+  static constexpr bool kExt = EXT_;
   using OutT = OutT_;
   static_assert(DQK % 64 == 0 && DQK >= 64 && DQK <= 256, "d_qk must be 64..256 in steps of 64");
   static_assert(DV == 64 || DV == 128, "d_v must be 64 or 128");
@@ -248,6 +257,11 @@ struct Waiter {
   }
 };
 
+__device__ __forceinline__ int key_hi(const Params& p, int t) {
+  return p.key_map ? compressed_limit(t, p.T, p.kv_len) : t;
+}
+__device__ __forceinline__ int key_lo(const Params& p, int t) { return p.window > 0 ? t - p.window + 1 : INT_MIN / 2; }
+
 __device__ __forceinline__ uint8_t* smem_base() {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t a = ptx::smem_u32(smem_raw);
@@ -280,6 +294,7 @@ __device__ __forceinline__ int fetch_row_entry(const Params& p, int u, int lane)
 }
 
 // `idx0` is entry `lane` of the unit's selection row (fetch_row_entry).
+template <bool EXT>
 __device__ int build_unit_info(const Params& p, int u, int* inf, int lane, int idx0) {
   const int per_bkv = (p.qb_end - p.qb_begin) * p.parts;
   const int bkv_off = u / per_bkv;
@@ -291,7 +306,7 @@ __device__ int build_unit_info(const Params& p, int u, int* inf, int lane, int i
   const int b = bkv / p.Hkv, kvh = bkv - b * p.Hkv;
   const int t0 = qb * p.BQ + part * p.BQs;
   const int ntok = max(0, min(p.BQs, p.T - t0));
-  int seq0 = 0, kend = p.T;
+  int seq0 = 0, kend = p.kv_len;
   if (p.cu_seqlens != nullptr && ntok > 0) {
     int lo = 0, hi = p.n_seq;
     while (hi - lo > 1) {
@@ -301,7 +316,9 @@ __device__ int build_unit_info(const Params& p, int u, int* inf, int lane, int i
     seq0 = __ldg(p.cu_seqlens + lo);
     kend = __ldg(p.cu_seqlens + lo + 1);
   }
-  const int lim = min(t0 + ntok - 1, kend - 1);  // last key position any row of the unit may see
+  // last key position any row of the unit may see; first key position any row may see
+  const int lim = min(EXT ? key_hi(p, t0 + ntok - 1) : t0 + ntok - 1, kend - 1);
+  const int low = EXT ? key_lo(p, t0) : 0;
   const int nblk = (kend - seq0 + p.LP - 1) / p.LP;
   const int spb = p.LP / kSub;
   const int32_t* row = p.sel + ((size_t)bkv * p.NQB + qb) * p.KSEL;
@@ -311,6 +328,7 @@ __device__ int build_unit_info(const Params& p, int u, int* inf, int lane, int i
       const int j = base + lane;
       const int idx = base == 0 ? idx0 : ((j < p.KSEL) ? __ldg(row + j) : -1);
       bool valid = idx >= 0 && idx < nblk && (seq0 + idx * p.LP) <= lim;
+      if (EXT) valid = valid && (seq0 + idx * p.LP + p.LP - 1) >= low;
       // set semantics: drop repeats of an earlier entry (same 32-entry group)
       if ((__match_any_sync(0xffffffffu, idx) & ((1u << lane) - 1u)) != 0u) valid = false;
       if (valid && base > 0) {  // earlier groups (KSEL > 32 only)
@@ -369,7 +387,7 @@ __device__ void scheduler_role(const CUtensorMap* tmQ, const Params& p, uint8_t*
       if (!__shfl_sync(0xffffffffu, r, 0)) break;
     }
     int* inf = info_slot(p, smem, info.idx);
-    const int nsub = build_unit_info(p, u, inf, lane, idx);
+    const int nsub = build_unit_info<C::kExt>(p, u, inf, lane, idx);
     __syncwarp();
     if (lane == 0) ptx::mbar_arrive(&bars->info_full[info.idx]);
     info.next(kInfoSlots);
@@ -694,6 +712,14 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, SmemBars* bars, con
       continue;
     }
     const int tcol = t0 + col_i;
+    // extended visibility only: this row's visible keys, and the keys every row of the unit sees
+    int hi_col = tcol, lo_col = 0, hi_all = t0, lo_all = 0;
+    if constexpr (C::kExt) {
+      hi_col = key_hi(p, tcol);
+      lo_col = key_lo(p, tcol);
+      hi_all = key_hi(p, t0);
+      lo_all = key_lo(p, t0 + p.BQs - 1);
+    }
     const uint32_t obase = tmem + lane_addr + C::kTmemO + (wg * 2 + (ne & 1)) * NCOL;
     float m_run = -INFINITY, l_run = 0.f;
     bool first = true, quit = false;
@@ -720,7 +746,11 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, SmemBars* bars, con
       const int s0 = inf[kInfoHdr + 2 * c];
       const bool has1 = (2 * c + 1) < nsub;
       const int s1 = has1 ? inf[kInfoHdr + 2 * c + 1] : 0;
-      const bool full = has1 && (max(s0, s1) + kSub - 1 <= t0) && (max(s0, s1) + kSub <= kend);
+      bool full;
+      if constexpr (C::kExt)
+        full = has1 && (max(s0, s1) + kSub - 1 <= hi_all) && (max(s0, s1) + kSub <= kend) && (min(s0, s1) >= lo_all);
+      else
+        full = has1 && (max(s0, s1) + kSub - 1 <= t0) && (max(s0, s1) + kSub <= kend);
       float sc[KPT];
 #pragma unroll
       for (int q4 = 0; q4 < KPT / 4; ++q4) {
@@ -738,7 +768,11 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, SmemBars* bars, con
             const int key = 4 * TPC * q4 + 4 * kg + j;
             const int sb = key >> 6;
             const int kpos = (sb ? s1 : s0) + (key & 63);
-            const bool valid = (sb == 0 || has1) && kpos <= tcol && kpos < kend;
+            bool valid;
+            if constexpr (C::kExt)
+              valid = (sb == 0 || has1) && kpos <= hi_col && kpos >= lo_col && kpos < kend;
+            else
+              valid = (sb == 0 || has1) && kpos <= tcol && kpos < kend;
             if (!valid) sc[4 * q4 + j] = -INFINITY;
           }
         }

@@ -171,6 +171,54 @@ std::vector<torch::Tensor> forward_lse(torch::Tensor Q, torch::Tensor K, torch::
   return {O, L};
 }
 
+// Forward with the extended key visibility of nsa_sel_desc (window, compressed key map; K/V may
+// have kv_len != T rows with the compressed map): returns [O (fp32), LSE].
+std::vector<torch::Tensor> forward_ext(torch::Tensor Q, torch::Tensor K, torch::Tensor V, torch::Tensor sel,
+                                       int64_t l_prime, int64_t BQ, int64_t window, int64_t key_map, double scale) {
+  TORCH_CHECK(Q.is_cuda() && K.is_cuda() && V.is_cuda() && sel.is_cuda(), "Q, K, V and sel must be CUDA tensors");
+  TORCH_CHECK(Q.scalar_type() == at::kBFloat16 && K.scalar_type() == at::kBFloat16 &&
+                  V.scalar_type() == at::kBFloat16,
+              "Q, K and V must be bfloat16");
+  TORCH_CHECK(sel.scalar_type() == at::kInt, "sel must be int32");
+  TORCH_CHECK(Q.dim() == 4 && K.dim() == 4 && V.dim() == 4 && sel.dim() == 4,
+              "expected Q [B,Hq,T,d], K/V [B,Hkv,kv_len,d] and sel [B,Hkv,NQB,KSEL]");
+  TORCH_CHECK(Q.is_contiguous() && K.is_contiguous() && V.is_contiguous() && sel.is_contiguous(),
+              "Q, K, V and sel must be contiguous");
+  TORCH_CHECK(K.size(0) == Q.size(0) && V.size(0) == Q.size(0) && sel.size(0) == Q.size(0), "batch mismatch");
+  TORCH_CHECK(V.size(2) == K.size(2) && V.size(1) == K.size(1) && sel.size(1) == K.size(1), "K/V shape mismatch");
+  TORCH_CHECK(K.size(3) == Q.size(3), "Q and K head dims differ");
+  const Api& a = api();
+  const c10::cuda::CUDAGuard guard(Q.device());
+  auto O = torch::empty({Q.size(0), Q.size(1), Q.size(2), V.size(3)}, Q.options().dtype(torch::kFloat32));
+  auto L = torch::empty({Q.size(0), Q.size(1), Q.size(2)}, Q.options().dtype(torch::kFloat32));
+  nsa_sel_desc d;
+  memset(&d, 0, sizeof(d));
+  d.q = Q.data_ptr();
+  d.k = K.data_ptr();
+  d.v = V.data_ptr();
+  d.sel = sel.data_ptr<int32_t>();
+  d.o = O.data_ptr();
+  d.lse = L.data_ptr<float>();
+  d.batch = i32(Q.size(0), "B");
+  d.heads_q = i32(Q.size(1), "Hq");
+  d.heads_kv = i32(K.size(1), "Hkv");
+  d.seq_len = i32(Q.size(2), "T");
+  d.kv_len = i32(K.size(2), "kv_len");
+  d.d_qk = i32(Q.size(3), "d_qk");
+  d.d_v = i32(V.size(3), "d_v");
+  d.n_qblocks = i32(sel.size(2), "NQB");
+  d.n_sel = i32(sel.size(3), "KSEL");
+  d.block_size = i32(l_prime, "l_prime");
+  d.q_block = i32(BQ, "BQ");
+  d.window = i32(window, "window");
+  d.key_map = i32(key_map, "key_map");
+  d.o_dtype = NSA_DTYPE_F32;
+  d.scale = static_cast<float>(scale);
+  const int rc = a.run(&d, reinterpret_cast<nsa_stream_t>(c10::cuda::getCurrentCUDAStream().stream()));
+  if (rc != NSA_OK) TORCH_CHECK(false, format_msg("nsa_sel_run failed (%d): %s", rc, a.last_error()));
+  return {O, L};
+}
+
 // Block selection (nsa_sel_select): sel int32 [B, Hkv, T, min(n_sel, ceil(T/l_prime))].
 torch::Tensor select_blocks(torch::Tensor Q, torch::Tensor K, int64_t n_sel, int64_t l_prime, int64_t cmp_block,
                             int64_t cmp_stride) {
@@ -206,6 +254,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("forward_lse", &forward_lse, "forward_lse(Q, K, V, sel, l_prime, BQ, cu_seqlens, scale, out_f32) -> [O, LSE]",
         py::arg("Q"), py::arg("K"), py::arg("V"), py::arg("sel"), py::arg("l_prime"), py::arg("BQ"),
         py::arg("cu_seqlens") = py::none(), py::arg("scale") = 0.0, py::arg("out_f32") = false);
+  m.def("forward_ext", &forward_ext,
+        "forward_ext(Q, K, V, sel, l_prime, BQ, window, key_map, scale) -> [O fp32, LSE]", py::arg("Q"), py::arg("K"),
+        py::arg("V"), py::arg("sel"), py::arg("l_prime"), py::arg("BQ"), py::arg("window") = 0,
+        py::arg("key_map") = 0, py::arg("scale") = 0.0);
   m.def("select_blocks", &select_blocks, "select_blocks(Q, K, n_sel, l_prime, cmp_block, cmp_stride) -> sel int32",
         py::arg("Q"), py::arg("K"), py::arg("n_sel"), py::arg("l_prime"), py::arg("cmp_block") = 32,
         py::arg("cmp_stride") = 16);

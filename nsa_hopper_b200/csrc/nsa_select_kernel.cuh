@@ -24,6 +24,7 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 #include <math.h>
+#include "nsa_linspace.cuh"
 
 namespace nsa {
 namespace select {
@@ -35,29 +36,9 @@ constexpr int kMaxK = 32;       // top-k capacity (one list entry per lane)
 constexpr int kMaxD = 256;
 
 // Selection block of compressed key i: floor(linspace(0, T-1, n_cmp)[i] / l_prime), clamped to
-// n_blk - 1 (nsa_reference.py:35-36).  The float32 linspace value is formed as PyTorch's CPU
-// kernel forms it (step rounded to float32, value computed in double from the nearer end, then
-// rounded) and the floor division follows PyTorch's float floor-divide; explicit _rn
-// intrinsics keep the compiler from fusing the products into FMAs.
-__device__ __forceinline__ float linspace_f32(int i, int T, int n) {
-  if (n == 1) return 0.f;
-  const float step = __fdiv_rn((float)(T - 1), (float)(n - 1));
-  if (i < n / 2) return (float)__dmul_rn((double)step, (double)i);
-  return (float)__dsub_rn((double)(T - 1), __dmul_rn((double)step, (double)(n - 1 - i)));
-}
-__device__ __forceinline__ float floor_div_f32(float a, float b) {
-  const float mod = fmodf(a, b);
-  float div = __fdiv_rn(__fsub_rn(a, mod), b);
-  if (mod != 0.f && ((b < 0.f) != (mod < 0.f))) div = __fsub_rn(div, 1.f);
-  if (div != 0.f) {
-    float fl = floorf(div);
-    if (__fsub_rn(div, fl) > 0.5f) fl = __fadd_rn(fl, 1.f);
-    return fl;
-  }
-  return copysignf(0.f, __fdiv_rn(a, b));
-}
+// n_blk - 1 (nsa_reference.py:35-36); see nsa_linspace.cuh.
 __device__ __forceinline__ int cmp_block_of(int i, int T, int n_cmp, int l_prime, int n_blk) {
-  const int nb = (int)floor_div_f32(linspace_f32(i, T, n_cmp), (float)l_prime);
+  const int nb = (int)nsa::floor_div_f32(nsa::linspace_f32(i, T, n_cmp), (float)l_prime);
   return nb < n_blk - 1 ? nb : n_blk - 1;
 }
 

@@ -1,11 +1,13 @@
 """Full NSA forward around the B200 selected-branch kernel.
 
 This is the caller the reference's ``validate.check(fn)`` drives (validate.py:12-28): the three
-NSA branches and the learned gate of ``nsa_forward`` (nsa_reference.py:46-89), with the
-selected branch computed by the sm_100a kernel (``ops.forward``) and the compressed and
-sliding-window branches, the compression and the block scoring written with PyTorch tensor
-ops on the same device.  Semantics follow the reference line for line where it matters for
-results:
+NSA branches and the learned gate of ``nsa_forward`` (nsa_reference.py:46-89).  On the GPU all
+three attention branches run on the sm_100a kernel: the selected branch with the selection
+kernel's (or the given) index rows, the sliding-window branch with per-token rows covering the
+window and the kernel's window bound, the compressed branch over the mean-pooled keys with the
+kernel's compressed key map.  The tensor-op functions below (``compressed_branch``,
+``window_branch``, ``block_scores``, ``select_blocks``) restate the same branches for CPU tests
+and cross-checks.  Semantics follow the reference line for line where it matters for results:
 
 * compression: overlapping mean pooling of ``cmp_block`` keys every ``cmp_stride``
   (nsa_reference.py:5-16);
@@ -130,6 +132,48 @@ def select_blocks(Q: torch.Tensor, Kc: torch.Tensor, n_sel: int, l_prime: int, c
     return out
 
 
+def window_selection(B: int, Hkv: int, T: int, window: int, l_prime: int, device) -> torch.Tensor:
+    """Per-token selection rows covering keys [t - window + 1, t]: blocks t//l' down to
+    (t - window + 1)//l' (-1 padding), int32 [B, Hkv, T, (window - 1)//l' + 2]."""
+    nw = (window - 1) // l_prime + 2
+    cur = torch.arange(T, device=device, dtype=torch.int32) // l_prime
+    sel = cur.view(-1, 1) - torch.arange(nw, device=device, dtype=torch.int32).view(1, -1)
+    sel = torch.where(sel >= 0, sel, torch.full_like(sel, -1))
+    return sel.view(1, 1, T, nw).expand(B, Hkv, T, nw).contiguous()
+
+
+def compressed_selection(B: int, Hkv: int, T: int, n_cmp: int, device) -> torch.Tensor:
+    """Every 64-key block of the compressed keys, for every token: int32 [B, Hkv, T, ceil(n_cmp/64)]
+    (the kernel's compressed key map then hides the keys past each token's position)."""
+    nb = (n_cmp + 63) // 64
+    return torch.arange(nb, device=device, dtype=torch.int32).view(1, 1, 1, nb).expand(B, Hkv, T, nb).contiguous()
+
+
+def window_branch_kernel(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, window: int) -> torch.Tensor:
+    """The sliding-window branch on the B200 kernel (bf16 inputs, fp32 O)."""
+    from . import ops
+
+    B, Hq, T, _ = Q.shape
+    sel = window_selection(B, K.shape[1], T, window, 64, Q.device)
+    o, _ = ops.forward_ext(Q, K, V, sel, 64, 1, window=window, key_map=0)
+    return o
+
+
+def compressed_branch_kernel(Q: torch.Tensor, Kc: torch.Tensor, Vc: torch.Tensor) -> torch.Tensor:
+    """The compressed branch on the B200 kernel: compressed keys/values (bf16) with the
+    compressed key map (key i visible to t iff float32 linspace(0, T-1, n_cmp)[i] <= t)."""
+    from . import ops
+
+    B, Hq, T, _ = Q.shape
+    n_cmp = Kc.shape[2]
+    if n_cmp == 0:
+        return torch.zeros(B, Hq, T, Vc.shape[3], dtype=torch.float32, device=Q.device)
+    sel = compressed_selection(B, Kc.shape[1], T, n_cmp, Q.device)
+    o, _ = ops.forward_ext(Q, Kc.to(torch.bfloat16).contiguous(), Vc.to(torch.bfloat16).contiguous(), sel, 64, 1,
+                           window=0, key_map=1)
+    return o
+
+
 def gate_weights(gate_w: Optional[torch.Tensor], device) -> torch.Tensor:
     if gate_w is None:
         return torch.full((3,), 1.0 / 3.0, dtype=torch.float32, device=device)
@@ -147,16 +191,15 @@ def nsa_forward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, *, n_sel: int
 
     if not Q.is_cuda:
         raise RuntimeError("nsa_forward needs CUDA tensors (the selected branch is a B200 kernel)")
-    Kc, Vc = compress_kv(K, V, cmp_block, cmp_stride)
-    o_cmp = compressed_branch(Q, Kc, Vc)
+    Qb, Kb, Vb = (x.to(torch.bfloat16).contiguous() for x in (Q, K, V))
+    Kc, Vc = compress_kv(Kb, Vb, cmp_block, cmp_stride)
+    o_cmp = compressed_branch_kernel(Qb, Kc, Vc)
     if sel_override is not None:
         sel = sel_override.to(device=Q.device, dtype=torch.int32).contiguous()
     else:  # the B200 selection kernel (scores in fp32, top-k per token)
-        sel = ops.select_blocks(Q.to(torch.bfloat16).contiguous(), K.to(torch.bfloat16).contiguous(), n_sel, l_prime,
-                                cmp_block, cmp_stride)
-    o_sel = ops.forward(Q.to(torch.bfloat16).contiguous(), K.to(torch.bfloat16).contiguous(),
-                        V.to(torch.bfloat16).contiguous(), sel, l_prime, 1)
-    o_win = window_branch(Q, K, V, window)
+        sel = ops.select_blocks(Qb, Kb, n_sel, l_prime, cmp_block, cmp_stride)
+    o_sel = ops.forward(Qb, Kb, Vb, sel, l_prime, 1)
+    o_win = window_branch_kernel(Qb, Kb, Vb, window)
     g = gate_weights(gate_w, Q.device)
     return g[0] * o_cmp + g[1] * o_sel + g[2] * o_win, sel
 

@@ -34,6 +34,15 @@ def forward_lse(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, sel: torch.Te
     return o, lse
 
 
+def forward_ext(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, sel: torch.Tensor, l_prime: int = 64, BQ: int = 1,
+                window: int = 0, key_map: int = 0, scale: float = 0.0) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Forward with extended key visibility (fp32 O, fp32 LSE): ``window`` > 0 limits query t to
+    keys p with t - p < window; ``key_map`` = 1 treats K/V as compressed keys (kv_len rows) visible
+    to t iff float32 linspace(0, T-1, kv_len)[i] <= t (the compressed branch of NSA)."""
+    o, lse = _C.forward_ext(Q, K, V, sel, int(l_prime), int(BQ), int(window), int(key_map), float(scale))
+    return o, lse
+
+
 def select_blocks(Q: torch.Tensor, K: torch.Tensor, n_sel: int, l_prime: int = 64, cmp_block: int = 32,
                   cmp_stride: int = 16) -> torch.Tensor:
     """Block selection on the GPU (nsa_sel_select): int32 [B, Hkv, T, min(n_sel, ceil(T/l_prime))],

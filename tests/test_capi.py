@@ -113,3 +113,29 @@ def test_select_workspace_bytes():
     assert capi.select_workspace_bytes(1, 4, 65536, 128, 64) == 4 * 1024 * 128 * 4
     assert capi.select_workspace_bytes(2, 2, 500, 64, 64) == 2 * 2 * 8 * 64 * 4
     assert capi.select_workspace_bytes(0, 2, 500, 64, 64) == -1
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(kv_len=-1), capi.NSA_ERR_INVALID_ARG),
+    (dict(window=-5), capi.NSA_ERR_INVALID_ARG),
+    (dict(key_map=2), capi.NSA_ERR_INVALID_ARG),
+    (dict(kv_len=4095), capi.NSA_ERR_INVALID_ARG),                        # kv_len != T needs the compressed map
+    (dict(kv_len=4095, key_map=1, window=64), capi.NSA_ERR_UNSUPPORTED),  # window + compressed map
+    (dict(window=64, cu_seqlens=256, n_seqs=1), capi.NSA_ERR_UNSUPPORTED),
+])
+def test_key_visibility_validation(kw, code):
+    with pytest.raises(capi.NsaSelError) as e:
+        capi.plan(_desc(**kw))
+    assert e.value.code == code
+
+
+def test_compressed_key_map_plan():
+    p = capi.plan(_desc(kv_len=4095, key_map=1, n_sel=64, o_dtype=capi.DTYPE_F32))
+    assert p["n_units"] == 4 * 65536
+
+
+def test_extended_visibility_needs_fp32_variant():
+    with pytest.raises(capi.NsaSelError) as e:
+        capi.plan(_desc(window=512))  # bf16 O: no window variant is built
+    assert e.value.code == capi.NSA_ERR_UNSUPPORTED
+    assert capi.plan(_desc(window=512, o_dtype=capi.DTYPE_F32))["n_cols"] == 16

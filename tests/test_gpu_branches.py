@@ -1,0 +1,70 @@
+"""The kernel's extended key visibility (sliding window; compressed keys with the float32
+linspace key map) against the tensor-op restatements of the reference's window and compressed
+branches (nsa_reference.py:59-64, 79-82), which tests/test_nsa_wrapper.py pins to the reference."""
+import numpy as np
+import pytest
+import torch
+
+from nsa_hopper_b200 import nsa, ops
+
+pytestmark = pytest.mark.gpu
+
+
+def _qkv(B, Hq, Hkv, T, D, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    mk = lambda h: torch.randn(B, h, T, D, device="cuda", generator=g).to(torch.bfloat16)
+    return mk(Hq), mk(Hkv), mk(Hkv)
+
+
+def _lse_masked(q, k, mask, scale):
+    G = q.shape[1] // k.shape[1]
+    s = torch.matmul(q.float(), k.float().repeat_interleave(G, 1).transpose(-1, -2)) * scale
+    s = s.masked_fill(~mask, float("-inf"))
+    return torch.logsumexp(s, -1)
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,T,D,window", [(1, 16, 2, 1500, 64, 128), (1, 8, 2, 777, 128, 100),
+                                                 (2, 4, 4, 512, 64, 512), (1, 64, 4, 2048, 128, 512),
+                                                 (1, 16, 1, 300, 64, 1000)])
+def test_window_branch_on_kernel(B, Hq, Hkv, T, D, window):
+    q, k, v = _qkv(B, Hq, Hkv, T, D, T + window)
+    sel = nsa.window_selection(B, Hkv, T, window, 64, q.device)
+    o, lse = ops.forward_ext(q, k, v, sel, 64, 1, window=window, key_map=0)
+    ref = nsa.window_branch(q, k, v, window)
+    torch.cuda.synchronize()
+    assert (o - ref).abs().max().item() <= 2e-2
+    t = torch.arange(T, device="cuda")
+    d = t.view(-1, 1) - t.view(1, -1)
+    mask = ((d >= 0) & (d < window)).view(1, 1, T, T)
+    want = _lse_masked(q, k, mask, D ** -0.5)
+    assert ((lse - want).abs() / want.abs().clamp(min=1)).max().item() <= 1e-3
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,T,D", [(1, 8, 2, 512, 64), (1, 16, 1, 1500, 64), (2, 8, 2, 1024, 128),
+                                          (1, 64, 4, 4096, 128), (1, 4, 4, 40, 64)])
+def test_compressed_branch_on_kernel(B, Hq, Hkv, T, D):
+    q, k, v = _qkv(B, Hq, Hkv, T, D, 3 * T)
+    Kc, Vc = nsa.compress_kv(k, v, 32, 16)
+    Kc, Vc = Kc.to(torch.bfloat16), Vc.to(torch.bfloat16)  # the kernel's operands
+    o = nsa.compressed_branch_kernel(q, Kc, Vc)
+    ref = nsa.compressed_branch(q, Kc.float(), Vc.float())
+    torch.cuda.synchronize()
+    assert (o - ref).abs().max().item() <= 2e-2
+    if Kc.shape[2] > 0:
+        sel = nsa.compressed_selection(B, Hkv, T, Kc.shape[2], q.device)
+        _, lse = ops.forward_ext(q, Kc, Vc, sel, 64, 1, window=0, key_map=1)
+        cpos = nsa.compressed_positions(T, Kc.shape[2], q.device)
+        mask = (cpos.view(1, -1) <= torch.arange(T, device="cuda", dtype=torch.float32).view(-1, 1))
+        want = _lse_masked(q, Kc, mask.view(1, 1, T, -1), D ** -0.5)
+        assert ((lse - want).abs() / want.abs().clamp(min=1)).max().item() <= 1e-3
+
+
+def test_window_covering_everything_equals_causal_attention():
+    B, Hq, Hkv, T, D = 1, 8, 2, 700, 64
+    q, k, v = _qkv(B, Hq, Hkv, T, D, 9)
+    nb = (T + 63) // 64
+    all_blocks = torch.arange(nb, device="cuda", dtype=torch.int32).view(1, 1, 1, nb).expand(B, Hkv, T, nb).contiguous()
+    o_w, l_w = ops.forward_ext(q, k, v, all_blocks, 64, 1, window=T, key_map=0)
+    o_c, l_c = ops.forward_ext(q, k, v, all_blocks, 64, 1, window=0, key_map=0)
+    torch.cuda.synchronize()
+    assert torch.equal(o_w, o_c) and torch.equal(l_w, l_c)

@@ -127,3 +127,29 @@ def test_selection_kernel_block_mapping_matches_reference(T):
     for lp in (64, 128, 256):
         want = (torch.from_numpy(ref) // lp).numpy()
         assert (_floor_div_f32_device_rule(mine, lp) == want).all()
+
+
+def _compressed_limit_device_rule(t, T, n):
+    """nsa_linspace.cuh: compressed_limit (the last compressed key visible to query t)."""
+    if n <= 1:
+        return n - 1
+    pos = _linspace_f32_device_rule(T, n)
+    est = int(np.floor(t * (n - 1) / (T - 1)))
+    best = -1
+    for i in range(max(0, est - 2), min(n - 1, est + 3) + 1):
+        if pos[i] <= np.float32(t):
+            best = i
+    return best
+
+
+@pytest.mark.parametrize("T", [40, 500, 1024, 2048, 4097, 65536])
+def test_compressed_key_map_matches_reference_mask(T):
+    """The kernel's compressed key map (key i visible to t iff linspace(i) <= t) is the reference's
+    cmask = cpos <= arange(S) (nsa_reference.py:62-63) for every (sampled) token."""
+    n = (T - 32) // 16 + 1
+    cpos = torch.linspace(0, T - 1, n)
+    assert (np.diff(cpos.numpy()) >= 0).all()
+    ts = range(T) if T <= 4097 else np.random.default_rng(0).integers(0, T, 3000)
+    for t in ts:
+        want = int((cpos <= torch.tensor(float(t))).sum().item()) - 1
+        assert _compressed_limit_device_rule(int(t), T, n) == want, t
