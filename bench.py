@@ -403,6 +403,67 @@ def run_select(args):
     }
 
 
+def run_nsa(args):
+    """--stage nsa: the full NSA forward (nsa_hopper_b200.nsa.nsa_forward: compression, the block
+    selection kernel, the selected / sliding-window / compressed branches on the attention kernel
+    and the gate) on the workload's shapes, window 512 and the reference's compression
+    (32 keys every 16).  Reports tokens/s of the whole layer and each stage's time."""
+    import torch
+
+    from nsa_hopper_b200 import nsa, ops, workload
+
+    w = workload.CONFIGS[args.config]
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    B, T, Hq, Hkv, D, lp, n = w.B, w.T, w.Hq, w.Hkv, w.d_qk, w.block, w.n
+    window = 512
+    gen = torch.Generator(device=dev).manual_seed(args.seed)
+    q = torch.randn(B, Hq, T, D, device=dev, generator=gen).to(torch.bfloat16)
+    k = torch.randn(B, Hkv, T, D, device=dev, generator=gen).to(torch.bfloat16)
+    v = torch.randn(B, Hkv, T, D, device=dev, generator=gen).to(torch.bfloat16)
+    flush = torch.empty(FLUSH_BYTES // 4, device=dev, dtype=torch.float32)
+    for _ in range(args.warmup):
+        nsa.nsa_forward(q, k, v, n_sel=n, l_prime=lp, window=window)
+    torch.cuda.synchronize()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
+    with ClockSampler(0) as clk:
+        for i in range(args.steps):
+            flush.fill_(float(i))
+            ev[i][0].record()
+            nsa.nsa_forward(q, k, v, n_sel=n, l_prime=lp, window=window)
+            ev[i][1].record()
+        torch.cuda.synchronize()
+    ms = statistics.mean(a.elapsed_time(b_) for a, b_ in ev)
+    # stage breakdown (one untimed-loop pass each, CUDA events)
+    stages = {}
+
+    def timed(name, fn):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        flush.fill_(0.0)
+        e0.record()
+        r = fn()
+        e1.record()
+        torch.cuda.synchronize()
+        stages[name] = round(e0.elapsed_time(e1), 3)
+        return r
+
+    Kc, Vc = timed("compress_kv", lambda: nsa.compress_kv(k, v, 32, 16))
+    sel = timed("select_kernel", lambda: ops.select_blocks(q, k, n, lp))
+    timed("selected_branch", lambda: ops.forward(q, k, v, sel, lp, 1))
+    timed("window_branch", lambda: nsa.window_branch_kernel(q, k, v, window))
+    timed("compressed_branch", lambda: nsa.compressed_branch_kernel(q, Kc, Vc))
+    return {
+        "metric": "NSA forward (3 branches + selection + gate) tokens/s", "value": B * T / (ms * 1e-3),
+        "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (fp32 branch outputs)",
+        "data": "synthetic N(0,1) bf16 Q/K/V",
+        "config": {"workload": args.config, "stage": "nsa", "B": B, "T": T, "Hq": Hq, "Hkv": Hkv, "d": D, "block": lp,
+                   "top_n": n, "window": window, "cmp_block": 32, "cmp_stride": 16,
+                   "l2": "256 MiB buffer written between timed steps (L2 flushed)"},
+        "stages_ms": stages, "e2e": None, "clocks": clk.summary(), "cpu_baseline": None,
+    }
+
+
 def cpu_baseline(args, seconds: float = 12.0):
     """Oracle (fp32, all host threads) on a bounded sample of the same workload: the last
     tokens of the sequence (full top-n cost), all KV heads.  Returns a dict."""
@@ -474,8 +535,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gather", action="store_true", help="skip the separately timed all-gather (N > 1)")
-    ap.add_argument("--stage", choices=["selected", "select"], default="selected",
-                    help="selected: the selected-branch forward (the headline); select: the block-selection kernel")
+    ap.add_argument("--stage", choices=["selected", "select", "nsa"], default="selected",
+                    help="selected: the selected-branch forward (the headline); select: the block-selection kernel; "
+                         "nsa: the full NSA forward")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -483,9 +545,9 @@ def main():
     rank = _env_int("RANK", 0)
     local_rank = _env_int("LOCAL_RANK", 0)
 
-    if args.stage == "select":
+    if args.stage in ("select", "nsa"):
         if rank == 0:
-            print(json.dumps(run_select(args)), flush=True)
+            print(json.dumps(run_select(args) if args.stage == "select" else run_nsa(args)), flush=True)
         return
 
     if args.impl == "reference":

@@ -101,7 +101,10 @@ typedef struct nsa_sel_desc {
   int32_t key_map;            /* NSA_KEYMAP_CAUSAL: key p visible to query t iff p <= t;
                                  NSA_KEYMAP_COMPRESSED: key i visible iff the float32
                                  linspace(0, seq_len-1, kv_len)[i] <= t (not with cu_seqlens) */
-  int32_t reserved[2];
+  /* Fused output combination (the NSA gate, reference nsa_reference.py:86-88): */
+  int32_t o_accumulate;       /* 0: O is overwritten; 1: O += w * result (fp32 O only; TMA reduce-add) */
+  int32_t reserved;
+  const float* o_weight;      /* optional device float w multiplying the result; NULL = 1 */
 } nsa_sel_desc;
 
 /* Launch plan chosen for a description (filled by nsa_sel_plan, used by the launcher). */

@@ -49,7 +49,9 @@ class NsaSelDesc(ctypes.Structure):
         ("kv_len", ctypes.c_int32),
         ("window", ctypes.c_int32),
         ("key_map", ctypes.c_int32),
-        ("reserved", ctypes.c_int32 * 2),
+        ("o_accumulate", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+        ("o_weight", ctypes.c_void_p),
     ]
 
 

@@ -194,6 +194,10 @@ int make_plan(const nsa_sel_desc* d, int sm_count, Plan* pl) {
     return fail(NSA_ERR_INVALID_ARG, "kv_len (%d) != seq_len (%d) needs key_map = NSA_KEYMAP_COMPRESSED", kv_len, T);
   if (d->key_map == NSA_KEYMAP_COMPRESSED && d->window > 0)
     return fail(NSA_ERR_UNSUPPORTED, "window and key_map = NSA_KEYMAP_COMPRESSED cannot be combined");
+  if (d->o_accumulate != 0 && d->o_accumulate != 1) return fail(NSA_ERR_INVALID_ARG, "o_accumulate must be 0 or 1");
+  if (d->o_accumulate && d->o_dtype != NSA_DTYPE_F32)
+    return fail(NSA_ERR_UNSUPPORTED, "o_accumulate needs fp32 O (o_dtype = NSA_DTYPE_F32)");
+  if ((reinterpret_cast<uintptr_t>(d->o_weight) & 3u) != 0) return fail(NSA_ERR_INVALID_ARG, "o_weight must be 4-byte aligned");
   if (d->cu_seqlens != nullptr && (d->window > 0 || d->key_map != NSA_KEYMAP_CAUSAL))
     return fail(NSA_ERR_UNSUPPORTED, "a varlen batch supports neither window nor key_map");
   if (d->cu_seqlens != nullptr) {
@@ -396,6 +400,8 @@ int launch(const nsa_sel_desc* d, nsa_stream_t stream) {
   p.key_map = d->key_map;
   p.debug_stall = (d->debug_flags & NSA_DEBUG_STALL) ? 1 : 0;
   p.out_bufs = pl.out_bufs;
+  p.o_accum = d->o_accumulate;
+  p.o_weight = d->o_weight;
 
   {
     std::lock_guard<std::mutex> lk(g_dev.mu);

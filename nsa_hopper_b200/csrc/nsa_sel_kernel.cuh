@@ -115,6 +115,8 @@ struct Params {
   int kv_len, window, key_map;
   int debug_stall;  // 1: the MMA warp first waits on a barrier nothing arrives on (error-path test)
   int out_bufs;     // output staging tiles (2: double buffer; 1 when shared memory is tight)
+  int o_accum;             // 1: O += w * result through TMA reduce-add (fp32 O); 0: O = w * result
+  const float* o_weight;   // device float w, or nullptr for 1
 };
 
 // P tiles: NP buffers (4 for N <= 32 and d_qk <= 128, else 2), NP / NWG per softmax group; the k-th chunk of
@@ -889,6 +891,7 @@ __device__ void epilogue_role(const CUtensorMap* tmO, const Params& p, uint8_t* 
   float* fac = reinterpret_cast<float*>(smem + p.off_fac);  // [wg][col]: merge weight / sum
   const float2* ml = reinterpret_cast<const float2*>(smem + p.off_ml);
   const int nrows = p.G * p.BQs;
+  const float wgt = p.o_weight != nullptr ? __ldg(p.o_weight) : 1.f;  // output weight (NSA gate)
   uint32_t ui = 0, ne = 0, st = 0;
   bool dead = false;
 
@@ -927,7 +930,7 @@ __device__ void epilogue_role(const CUtensorMap* tmO, const Params& p, uint8_t* 
       }
       const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
 #pragma unroll
-      for (int q = 0; q < NWG; ++q) fac[q * NCOL + i] = a[q] * inv;
+      for (int q = 0; q < NWG; ++q) fac[q * NCOL + i] = a[q] * (inv * wgt);
       const int cg = i / p.BQs, ci = i - (i / p.BQs) * p.BQs;
       if (i < nrows && ci < ntok && p.lse != nullptr) {
         const float lse = Ls > 0.f ? (M + log2f(Ls)) * 0.69314718055994530942f : -INFINITY;
@@ -973,8 +976,13 @@ __device__ void epilogue_role(const CUtensorMap* tmO, const Params& p, uint8_t* 
     if (i == 0) {
       if (ntok > 0) {
         OutT* stg = reinterpret_cast<OutT*>(smem + p.off_out + (p.out_bufs == 2 ? (st & 1) : 0u) * C::kOutBytes);
-        for (int dc = 0; dc < C::DV / 64; ++dc)
-          ptx::tma_store_4d(tmO, stg + dc * C::kOutChunkElems, dc * 64, t0, kvh * p.G, b);
+        if (p.o_accum) {
+          for (int dc = 0; dc < C::DV / 64; ++dc)
+            ptx::tma_reduce_add_4d(tmO, stg + dc * C::kOutChunkElems, dc * 64, t0, kvh * p.G, b);
+        } else {
+          for (int dc = 0; dc < C::DV / 64; ++dc)
+            ptx::tma_store_4d(tmO, stg + dc * C::kOutChunkElems, dc * 64, t0, kvh * p.G, b);
+        }
         ptx::bulk_commit();
       }
       ptx::mbar_arrive(&bars->info_empty[slot]);

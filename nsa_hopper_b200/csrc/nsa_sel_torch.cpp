@@ -174,7 +174,9 @@ std::vector<torch::Tensor> forward_lse(torch::Tensor Q, torch::Tensor K, torch::
 // Forward with the extended key visibility of nsa_sel_desc (window, compressed key map; K/V may
 // have kv_len != T rows with the compressed map): returns [O (fp32), LSE].
 std::vector<torch::Tensor> forward_ext(torch::Tensor Q, torch::Tensor K, torch::Tensor V, torch::Tensor sel,
-                                       int64_t l_prime, int64_t BQ, int64_t window, int64_t key_map, double scale) {
+                                       int64_t l_prime, int64_t BQ, int64_t window, int64_t key_map, double scale,
+                                       c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> weight,
+                                       bool accumulate, bool with_lse) {
   TORCH_CHECK(Q.is_cuda() && K.is_cuda() && V.is_cuda() && sel.is_cuda(), "Q, K, V and sel must be CUDA tensors");
   TORCH_CHECK(Q.scalar_type() == at::kBFloat16 && K.scalar_type() == at::kBFloat16 &&
                   V.scalar_type() == at::kBFloat16,
@@ -189,8 +191,24 @@ std::vector<torch::Tensor> forward_ext(torch::Tensor Q, torch::Tensor K, torch::
   TORCH_CHECK(K.size(3) == Q.size(3), "Q and K head dims differ");
   const Api& a = api();
   const c10::cuda::CUDAGuard guard(Q.device());
-  auto O = torch::empty({Q.size(0), Q.size(1), Q.size(2), V.size(3)}, Q.options().dtype(torch::kFloat32));
-  auto L = torch::empty({Q.size(0), Q.size(1), Q.size(2)}, Q.options().dtype(torch::kFloat32));
+  torch::Tensor O;
+  if (out.has_value()) {
+    O = *out;
+    TORCH_CHECK(O.is_cuda() && O.scalar_type() == at::kFloat && O.is_contiguous() && O.get_device() == Q.get_device(),
+                "out must be a contiguous fp32 CUDA tensor on Q's device");
+    TORCH_CHECK(O.dim() == 4 && O.size(0) == Q.size(0) && O.size(1) == Q.size(1) && O.size(2) == Q.size(2) &&
+                    O.size(3) == V.size(3),
+                "out must be [B, Hq, T, d_v]");
+  } else {
+    TORCH_CHECK(!accumulate, "accumulate needs an out tensor");
+    O = torch::empty({Q.size(0), Q.size(1), Q.size(2), V.size(3)}, Q.options().dtype(torch::kFloat32));
+  }
+  if (weight.has_value())
+    TORCH_CHECK(weight->is_cuda() && weight->scalar_type() == at::kFloat && weight->numel() >= 1 &&
+                    weight->get_device() == Q.get_device(),
+                "weight must be an fp32 CUDA tensor (its first element is used) on Q's device");
+  torch::Tensor L = with_lse ? torch::empty({Q.size(0), Q.size(1), Q.size(2)}, Q.options().dtype(torch::kFloat32))
+                             : torch::empty({0}, Q.options().dtype(torch::kFloat32));
   nsa_sel_desc d;
   memset(&d, 0, sizeof(d));
   d.q = Q.data_ptr();
@@ -198,7 +216,9 @@ std::vector<torch::Tensor> forward_ext(torch::Tensor Q, torch::Tensor K, torch::
   d.v = V.data_ptr();
   d.sel = sel.data_ptr<int32_t>();
   d.o = O.data_ptr();
-  d.lse = L.data_ptr<float>();
+  d.lse = with_lse ? L.data_ptr<float>() : nullptr;
+  d.o_accumulate = accumulate ? 1 : 0;
+  d.o_weight = weight.has_value() ? weight->data_ptr<float>() : nullptr;
   d.batch = i32(Q.size(0), "B");
   d.heads_q = i32(Q.size(1), "Hq");
   d.heads_kv = i32(K.size(1), "Hkv");
@@ -255,9 +275,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("Q"), py::arg("K"), py::arg("V"), py::arg("sel"), py::arg("l_prime"), py::arg("BQ"),
         py::arg("cu_seqlens") = py::none(), py::arg("scale") = 0.0, py::arg("out_f32") = false);
   m.def("forward_ext", &forward_ext,
-        "forward_ext(Q, K, V, sel, l_prime, BQ, window, key_map, scale) -> [O fp32, LSE]", py::arg("Q"), py::arg("K"),
-        py::arg("V"), py::arg("sel"), py::arg("l_prime"), py::arg("BQ"), py::arg("window") = 0,
-        py::arg("key_map") = 0, py::arg("scale") = 0.0);
+        "forward_ext(Q, K, V, sel, l_prime, BQ, window, key_map, scale, out, weight, accumulate, with_lse) -> "
+        "[O fp32, LSE]",
+        py::arg("Q"), py::arg("K"), py::arg("V"), py::arg("sel"), py::arg("l_prime"), py::arg("BQ"),
+        py::arg("window") = 0, py::arg("key_map") = 0, py::arg("scale") = 0.0, py::arg("out") = py::none(),
+        py::arg("weight") = py::none(), py::arg("accumulate") = false, py::arg("with_lse") = true);
   m.def("select_blocks", &select_blocks, "select_blocks(Q, K, n_sel, l_prime, cmp_block, cmp_stride) -> sel int32",
         py::arg("Q"), py::arg("K"), py::arg("n_sel"), py::arg("l_prime"), py::arg("cmp_block") = 32,
         py::arg("cmp_stride") = 16);

@@ -35,11 +35,19 @@ def forward_lse(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, sel: torch.Te
 
 
 def forward_ext(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, sel: torch.Tensor, l_prime: int = 64, BQ: int = 1,
-                window: int = 0, key_map: int = 0, scale: float = 0.0) -> Tuple[torch.Tensor, torch.Tensor]:
+                window: int = 0, key_map: int = 0, scale: float = 0.0, out: Optional[torch.Tensor] = None,
+                weight: Optional[torch.Tensor] = None, accumulate: bool = False,
+                with_lse: bool = True) -> Tuple[torch.Tensor, torch.Tensor]:
     """Forward with extended key visibility (fp32 O, fp32 LSE): ``window`` > 0 limits query t to
     keys p with t - p < window; ``key_map`` = 1 treats K/V as compressed keys (kv_len rows) visible
-    to t iff float32 linspace(0, T-1, kv_len)[i] <= t (the compressed branch of NSA)."""
-    o, lse = _C.forward_ext(Q, K, V, sel, int(l_prime), int(BQ), int(window), int(key_map), float(scale))
+    to t iff float32 linspace(0, T-1, kv_len)[i] <= t (the compressed branch of NSA).
+
+    Fused output combination: the result is multiplied by ``weight[0]`` (an fp32 CUDA tensor, read
+    on the device) and written to ``out``, or added into it when ``accumulate`` (TMA reduce-add),
+    so the NSA gate g_c*O_cmp + g_s*O_sel + g_w*O_win is three launches into one buffer.
+    ``with_lse=False`` skips the LSE (an empty tensor is returned in its place)."""
+    o, lse = _C.forward_ext(Q, K, V, sel, int(l_prime), int(BQ), int(window), int(key_map), float(scale), out, weight,
+                            bool(accumulate), bool(with_lse))
     return o, lse
 
 

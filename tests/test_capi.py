@@ -139,3 +139,19 @@ def test_extended_visibility_needs_fp32_variant():
         capi.plan(_desc(window=512))  # bf16 O: no window variant is built
     assert e.value.code == capi.NSA_ERR_UNSUPPORTED
     assert capi.plan(_desc(window=512, o_dtype=capi.DTYPE_F32))["n_cols"] == 16
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(o_accumulate=1), capi.NSA_ERR_UNSUPPORTED),                   # bf16 O cannot be accumulated
+    (dict(o_accumulate=2, o_dtype=capi.DTYPE_F32), capi.NSA_ERR_INVALID_ARG),
+    (dict(o_weight=258, o_dtype=capi.DTYPE_F32), capi.NSA_ERR_INVALID_ARG),  # misaligned weight pointer
+])
+def test_fused_output_validation(kw, code):
+    with pytest.raises(capi.NsaSelError) as e:
+        capi.plan(_desc(**kw))
+    assert e.value.code == code
+
+
+def test_fused_output_plan():
+    p = capi.plan(_desc(o_accumulate=1, o_weight=260, o_dtype=capi.DTYPE_F32))
+    assert p["n_cols"] == 16

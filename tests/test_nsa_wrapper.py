@@ -153,3 +153,20 @@ def test_compressed_key_map_matches_reference_mask(T):
     for t in ts:
         want = int((cpos <= torch.tensor(float(t))).sum().item()) - 1
         assert _compressed_limit_device_rule(int(t), T, n) == want, t
+
+
+@pytest.mark.parametrize("T,window,bq", [(1000, 512, 1), (1000, 512, 4), (777, 100, 8), (130, 1000, 2), (64, 64, 16)])
+def test_window_selection_rows_cover_exactly_the_window(T, window, bq):
+    """Each query block's row lists exactly the 64-key blocks that meet [t0 - window + 1, t1]
+    (t0, t1 the block's first and last tokens), in descending order, -1 padded."""
+    sel = nsa.window_selection(1, 1, T, window, 64, "cpu", bq)[0, 0].numpy()
+    assert sel.shape == ((T + bq - 1) // bq, (window + bq - 2) // 64 + 2)
+    for qb in range(sel.shape[0]):
+        t0, t1 = qb * bq, min(T, qb * bq + bq) - 1
+        want = list(range(t1 // 64, max(0, t0 - window + 1) // 64 - 1, -1))
+        row = [int(x) for x in sel[qb]]
+        assert row[:len(want)] == want and all(x == -1 for x in row[len(want):])
+
+
+def test_branch_q_block_fills_the_64_column_tile():
+    assert [nsa.branch_q_block(g) for g in (1, 4, 8, 16, 32, 64, 128)] == [64, 16, 8, 4, 2, 1, 1]
