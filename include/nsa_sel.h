@@ -138,6 +138,29 @@ int nsa_sel_forward_lse(const void* q, const void* k, const void* v, const int32
    and the wait bound.  Same reference op (nsa_v2.cu:147-170). */
 int nsa_sel_run(const nsa_sel_desc* desc, nsa_stream_t stream);
 
+/* Host buffers for nsa_sel_run_host (same layouts as the device buffers of the descriptor;
+   pinned host memory lets the copies overlap the kernel). */
+typedef struct nsa_sel_host_io {
+  const void* q;              /* [B, Hq, T, d_qk] bf16 */
+  const void* k;              /* [B, Hkv, kv_len, d_qk] bf16 */
+  const void* v;              /* [B, Hkv, kv_len, d_v] bf16 */
+  const int32_t* sel;         /* [B, Hkv, NQB, KSEL] */
+  void* o;                    /* [B, Hq, T, d_v], dtype o_dtype; receives O */
+  float* lse;                 /* optional [B, Hq, T]; receives the LSE when desc->lse is set */
+  int32_t token_slices;       /* query-block ranges per (b, kvh) row; 0 = automatic */
+  int32_t reserved[7];
+} nsa_sel_host_io;
+
+/* The same forward for a caller whose tensors live in host memory (the reference op takes
+   whatever tensors it is given, nsa_v2.cu:147-170): copies the inputs of the descriptor's shard
+   into its device buffers, runs the kernel and copies O (and LSE) back, pipelined over (b, kvh)
+   rows x token slices so that the host-to-device copy of slice i+1, the kernel on slice i and the
+   device-to-host copy of slice i-1 overlap (two library-owned copy streams, ordered against
+   `stream` with events; no device memory is allocated).  Asynchronous: the host outputs are
+   complete when `stream` reaches the point after this call.  o_accumulate must be 0;
+   cu_seqlens, when set, must already be in device memory. */
+int nsa_sel_run_host(const nsa_sel_desc* desc, const nsa_sel_host_io* io, nsa_stream_t stream);
+
 /* Validate a description and report the launch plan without touching the GPU.
    sm_count <= 0 means "query the current device". */
 int nsa_sel_plan(const nsa_sel_desc* desc, int32_t sm_count, nsa_sel_plan_info* out);

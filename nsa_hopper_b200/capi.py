@@ -66,6 +66,16 @@ class NsaSelPlanInfo(ctypes.Structure):
     ]
 
 
+class NsaSelHostIO(ctypes.Structure):
+    """Mirror of ``nsa_sel_host_io``."""
+
+    _fields_ = [
+        ("q", ctypes.c_void_p), ("k", ctypes.c_void_p), ("v", ctypes.c_void_p), ("sel", ctypes.c_void_p),
+        ("o", ctypes.c_void_p), ("lse", ctypes.c_void_p), ("token_slices", ctypes.c_int32),
+        ("reserved", ctypes.c_int32 * 7),
+    ]
+
+
 class NsaSelError(RuntimeError):
     def __init__(self, code: int, message: str):
         super().__init__(f"nsa_sel error {code}: {message}")
@@ -91,6 +101,8 @@ def load(path: Optional[str] = None) -> ctypes.CDLL:
     lib.nsa_sel_forward_lse.restype = ctypes.c_int
     lib.nsa_sel_run.argtypes = [ctypes.POINTER(NsaSelDesc), vp]
     lib.nsa_sel_run.restype = ctypes.c_int
+    lib.nsa_sel_run_host.argtypes = [ctypes.POINTER(NsaSelDesc), ctypes.POINTER(NsaSelHostIO), vp]
+    lib.nsa_sel_run_host.restype = ctypes.c_int
     lib.nsa_sel_plan.argtypes = [ctypes.POINTER(NsaSelDesc), i32, ctypes.POINTER(NsaSelPlanInfo)]
     lib.nsa_sel_plan.restype = ctypes.c_int
     lib.nsa_sel_last_error.argtypes = []
@@ -163,3 +175,18 @@ def select_noalloc(q: int, k: int, sel_out: int, B: int, Hq: int, Hkv: int, T: i
     """nsa_sel_select_noalloc: block selection with the library's static scratch (no allocation)."""
     check(load().nsa_sel_select_noalloc(ctypes.c_void_p(q), ctypes.c_void_p(k), ctypes.c_void_p(sel_out), B, Hq,
                                         Hkv, T, d, l_prime, n_sel, cmp_block, cmp_stride, ctypes.c_void_p(stream)))
+
+
+def make_host_io(**kw) -> NsaSelHostIO:
+    io = NsaSelHostIO()
+    ctypes.memset(ctypes.addressof(io), 0, ctypes.sizeof(io))
+    for key, val in kw.items():
+        if not hasattr(io, key):
+            raise KeyError(key)
+        setattr(io, key, val)
+    return io
+
+
+def run_host(desc: NsaSelDesc, io: NsaSelHostIO, stream: int = 0) -> None:
+    """nsa_sel_run_host: host inputs in, host outputs back, copies pipelined with the kernel."""
+    check(load().nsa_sel_run_host(ctypes.byref(desc), ctypes.byref(io), ctypes.c_void_p(stream)))

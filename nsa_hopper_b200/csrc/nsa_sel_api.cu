@@ -466,9 +466,138 @@ int select_shape(int32_t B, int32_t Hq, int32_t Hkv, int32_t T, int32_t d, int32
   return NSA_OK;
 }
 
+// ------------------------------------------------------------------ host-buffer pipeline
+constexpr int kMaxSlices = 64;
+struct HostPipe {
+  bool ready = false;
+  cudaStream_t h2d = nullptr, d2h = nullptr;
+  cudaEvent_t entry = nullptr, done = nullptr;
+  cudaEvent_t in[kMaxSlices] = {}, out[kMaxSlices] = {};
+};
+std::mutex g_pipe_mu;
+HostPipe g_pipe[kMaxDevices];
+
+int pipe_for(int dev, HostPipe** out) {
+  HostPipe& hp = g_pipe[dev];
+  if (!hp.ready) {
+    cudaError_t e = cudaStreamCreateWithFlags(&hp.h2d, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&hp.d2h, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&hp.entry, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&hp.done, cudaEventDisableTiming);
+    for (int i = 0; i < kMaxSlices && e == cudaSuccess; ++i) {
+      e = cudaEventCreateWithFlags(&hp.in[i], cudaEventDisableTiming);
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&hp.out[i], cudaEventDisableTiming);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "creating the host pipeline's streams and events");
+    hp.ready = true;
+  }
+  *out = &hp;
+  return NSA_OK;
+}
+
+// G rows of `width` bytes, `pitch` apart, at the same offset in both buffers.
+cudaError_t copy_rows(void* dst, const void* src, size_t off, size_t width, size_t pitch, int rows,
+                      cudaMemcpyKind kind, cudaStream_t s) {
+  return cudaMemcpy2DAsync(static_cast<char*>(dst) + off, pitch, static_cast<const char*>(src) + off, pitch, width,
+                           (size_t)rows, kind, s);
+}
+
+int run_host(const nsa_sel_desc* d, const nsa_sel_host_io* io, nsa_stream_t stream) {
+  if (io == nullptr) return fail(NSA_ERR_INVALID_ARG, "io is NULL");
+  if (io->q == nullptr || io->k == nullptr || io->v == nullptr || io->sel == nullptr || io->o == nullptr)
+    return fail(NSA_ERR_INVALID_ARG, "io->q, k, v, sel and o must be non-NULL");
+  if (io->token_slices < 0) return fail(NSA_ERR_INVALID_ARG, "token_slices must be >= 0");
+  if (d != nullptr && d->o_accumulate != 0)
+    return fail(NSA_ERR_UNSUPPORTED, "o_accumulate is not supported with host buffers");
+  int sm = 0, dev = 0;
+  int rc = current_sm_count(&sm, &dev);
+  if (rc != NSA_OK) return rc;
+  Plan pl;
+  rc = make_plan(d, sm, &pl);
+  if (rc != NSA_OK) return rc;
+
+  const int Hq = d->heads_q, Hkv = d->heads_kv, T = d->seq_len, G = pl.G, BQ = d->q_block, NQB = d->n_qblocks;
+  const size_t KVL = (size_t)(d->kv_len > 0 ? d->kv_len : T);
+  const size_t qrow = (size_t)d->d_qk * 2, orow = (size_t)d->d_v * (d->o_dtype == NSA_DTYPE_F32 ? 4 : 2);
+  const size_t krow = (size_t)d->d_qk * 2, vrow = (size_t)d->d_v * 2, srow = (size_t)d->n_sel * 4;
+  const int rows = pl.bkv_end - pl.bkv_begin, nqb = pl.qb_end - pl.qb_begin;
+  int per_row = io->token_slices > 0 ? io->token_slices : (16 + rows - 1) / rows;
+  per_row = per_row < nqb ? per_row : nqb;
+  while (per_row > 1 && rows * per_row > kMaxSlices) --per_row;
+  if (rows * per_row > kMaxSlices) per_row = 1;
+  const bool lse = d->lse != nullptr && io->lse != nullptr;
+
+  std::lock_guard<std::mutex> lk(g_pipe_mu);
+  HostPipe* hp = nullptr;
+  rc = pipe_for(dev, &hp);
+  if (rc != NSA_OK) return rc;
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaEventRecord(hp->entry, cs);  // the copies follow earlier work on `stream`
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(hp->h2d, hp->entry, 0);
+  if (e != cudaSuccess) return cuda_fail(e, "ordering the host pipeline after the stream");
+  int slice = 0;
+  const int nslices = rows * per_row;
+  for (int r = pl.bkv_begin; r < pl.bkv_end; ++r) {
+    const int b = r / Hkv, kvh = r - (r / Hkv) * Hkv;
+    for (int j = 0; j < per_row; ++j, ++slice) {
+      const int qa = pl.qb_begin + (int)((long long)nqb * j / per_row);
+      const int qe = pl.qb_begin + (int)((long long)nqb * (j + 1) / per_row);
+      const int ta = qa * BQ, te = qe * BQ < T ? qe * BQ : T;
+      const size_t head0 = ((size_t)b * Hq + (size_t)kvh * G) * T + ta;  // first (head, token) row
+      if (j == 0) {  // the whole K/V row before the row's first kernel
+        e = cudaMemcpyAsync(static_cast<char*>(const_cast<void*>(d->k)) + (size_t)r * KVL * krow,
+                            static_cast<const char*>(io->k) + (size_t)r * KVL * krow, KVL * krow,
+                            cudaMemcpyHostToDevice, hp->h2d);
+        if (e == cudaSuccess)
+          e = cudaMemcpyAsync(static_cast<char*>(const_cast<void*>(d->v)) + (size_t)r * KVL * vrow,
+                              static_cast<const char*>(io->v) + (size_t)r * KVL * vrow, KVL * vrow,
+                              cudaMemcpyHostToDevice, hp->h2d);
+        if (e != cudaSuccess) return cuda_fail(e, "copying K/V to the device");
+      }
+      e = copy_rows(const_cast<void*>(d->q), io->q, head0 * qrow, (size_t)(te - ta) * qrow, (size_t)T * qrow, G,
+                    cudaMemcpyHostToDevice, hp->h2d);
+      if (e == cudaSuccess) {
+        const size_t so = ((size_t)r * NQB + qa) * srow;
+        e = cudaMemcpyAsync(reinterpret_cast<char*>(const_cast<int32_t*>(d->sel)) + so,
+                            reinterpret_cast<const char*>(io->sel) + so, (size_t)(qe - qa) * srow,
+                            cudaMemcpyHostToDevice, hp->h2d);
+      }
+      if (e == cudaSuccess) e = cudaEventRecord(hp->in[slice], hp->h2d);
+      if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, hp->in[slice], 0);
+      if (e != cudaSuccess) return cuda_fail(e, "copying Q/sel to the device");
+      nsa_sel_desc ds = *d;
+      ds.bkv_begin = r;
+      ds.bkv_end = r + 1;
+      ds.qb_begin = qa;
+      ds.qb_end = qe;
+      rc = launch(&ds, stream);
+      if (rc != NSA_OK) return rc;
+      e = cudaEventRecord(hp->out[slice], cs);
+      if (e == cudaSuccess) e = cudaStreamWaitEvent(hp->d2h, hp->out[slice], 0);
+      if (e == cudaSuccess)
+        e = copy_rows(io->o, d->o, head0 * orow, (size_t)(te - ta) * orow, (size_t)T * orow, G,
+                      cudaMemcpyDeviceToHost, hp->d2h);
+      if (e == cudaSuccess && lse)
+        e = copy_rows(io->lse, d->lse, head0 * 4, (size_t)(te - ta) * 4, (size_t)T * 4, G, cudaMemcpyDeviceToHost,
+                      hp->d2h);
+      if (e != cudaSuccess) return cuda_fail(e, "copying O/LSE to the host");
+    }
+  }
+  (void)nslices;
+  e = cudaEventRecord(hp->done, hp->d2h);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, hp->done, 0);
+  if (e != cudaSuccess) return cuda_fail(e, "ordering the stream after the host pipeline");
+  g_last_error[0] = '\0';
+  return NSA_OK;
+}
+
 }  // namespace
 
 extern "C" {
+
+int nsa_sel_run_host(const nsa_sel_desc* desc, const nsa_sel_host_io* io, nsa_stream_t stream) {
+  return run_host(desc, io, stream);
+}
 
 int64_t nsa_sel_select_workspace_bytes(int32_t B, int32_t Hkv, int32_t T, int32_t d, int32_t l_prime) {
   if (B <= 0 || Hkv <= 0 || T <= 0 || d <= 0 || l_prime <= 0) return -1;

@@ -18,7 +18,7 @@ def _desc(**kw):
 def test_library_exports_every_header_function():
     lib = capi.load()
     names = capi.header_functions()
-    assert set(names) >= {"nsa_sel_forward", "nsa_sel_forward_lse", "nsa_sel_run", "nsa_sel_plan",
+    assert set(names) >= {"nsa_sel_forward", "nsa_sel_forward_lse", "nsa_sel_run", "nsa_sel_run_host", "nsa_sel_plan",
                           "nsa_sel_last_error", "nsa_sel_version"}
     for n in names:
         assert hasattr(lib, n), n
@@ -29,19 +29,24 @@ def test_struct_layout_matches_header(tmp_path):
     """The ctypes mirrors have the size and field offsets the C compiler gives the header's structs."""
     fields = [f for f, _ in capi.NsaSelDesc._fields_]
     pfields = [f for f, _ in capi.NsaSelPlanInfo._fields_]
+    hfields = [f for f, _ in capi.NsaSelHostIO._fields_]
     src = tmp_path / "layout.c"
     lines = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{capi.HEADER_PATH}"', "int main(void) {",
-             'printf("%zu\\n", sizeof(nsa_sel_desc));', 'printf("%zu\\n", sizeof(nsa_sel_plan_info));']
+             'printf("%zu\\n", sizeof(nsa_sel_desc));', 'printf("%zu\\n", sizeof(nsa_sel_plan_info));',
+             'printf("%zu\\n", sizeof(nsa_sel_host_io));']
     lines += [f'printf("%zu\\n", offsetof(nsa_sel_desc, {f}));' for f in fields]
     lines += [f'printf("%zu\\n", offsetof(nsa_sel_plan_info, {f}));' for f in pfields]
+    lines += [f'printf("%zu\\n", offsetof(nsa_sel_host_io, {f}));' for f in hfields]
     lines += ["return 0; }"]
     src.write_text("\n".join(lines))
     exe = tmp_path / "layout"
     subprocess.run(["gcc", "-o", str(exe), str(src)], check=True)
     vals = [int(x) for x in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split()]
     assert vals[0] == ctypes.sizeof(capi.NsaSelDesc) and vals[1] == ctypes.sizeof(capi.NsaSelPlanInfo)
-    got = vals[2:]
+    assert vals[2] == ctypes.sizeof(capi.NsaSelHostIO)
+    got = vals[3:]
     want = [getattr(capi.NsaSelDesc, f).offset for f in fields] + [getattr(capi.NsaSelPlanInfo, f).offset for f in pfields]
+    want += [getattr(capi.NsaSelHostIO, f).offset for f in hfields]
     assert got == want
 
 
@@ -155,3 +160,16 @@ def test_fused_output_validation(kw, code):
 def test_fused_output_plan():
     p = capi.plan(_desc(o_accumulate=1, o_weight=260, o_dtype=capi.DTYPE_F32))
     assert p["n_cols"] == 16
+
+
+def test_host_path_validation():
+    """nsa_sel_run_host rejects bad host descriptions before touching the GPU (no device here:
+    the device query fails after the argument checks, so only argument errors are asserted)."""
+    lib = capi.load()
+    d = _desc(o_dtype=capi.DTYPE_F32, o_accumulate=1)
+    io = capi.make_host_io(q=256, k=256, v=256, sel=256, o=256)
+    assert lib.nsa_sel_run_host(ctypes.byref(d), None, None) == capi.NSA_ERR_INVALID_ARG
+    assert lib.nsa_sel_run_host(ctypes.byref(d), ctypes.byref(capi.make_host_io(q=256)), None) == capi.NSA_ERR_INVALID_ARG
+    assert lib.nsa_sel_run_host(ctypes.byref(d), ctypes.byref(io), None) == capi.NSA_ERR_UNSUPPORTED
+    io.token_slices = -1
+    assert lib.nsa_sel_run_host(ctypes.byref(_desc()), ctypes.byref(io), None) == capi.NSA_ERR_INVALID_ARG
