@@ -101,8 +101,9 @@ def load(path: Optional[str] = None) -> ctypes.CDLL:
     lib.nsa_sel_forward_lse.restype = ctypes.c_int
     lib.nsa_sel_run.argtypes = [ctypes.POINTER(NsaSelDesc), vp]
     lib.nsa_sel_run.restype = ctypes.c_int
-    lib.nsa_sel_run_host.argtypes = [ctypes.POINTER(NsaSelDesc), ctypes.POINTER(NsaSelHostIO), vp]
-    lib.nsa_sel_run_host.restype = ctypes.c_int
+    if hasattr(lib, "nsa_sel_run_host"):  # absent from builds that predate it
+        lib.nsa_sel_run_host.argtypes = [ctypes.POINTER(NsaSelDesc), ctypes.POINTER(NsaSelHostIO), vp]
+        lib.nsa_sel_run_host.restype = ctypes.c_int
     lib.nsa_sel_plan.argtypes = [ctypes.POINTER(NsaSelDesc), i32, ctypes.POINTER(NsaSelPlanInfo)]
     lib.nsa_sel_plan.restype = ctypes.c_int
     lib.nsa_sel_last_error.argtypes = []

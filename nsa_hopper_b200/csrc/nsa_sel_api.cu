@@ -65,6 +65,30 @@ struct DeviceCache {
 };
 DeviceCache g_dev;
 
+}  // namespace
+
+// Unit counters of the dynamic work distribution (Params::work_counter): one 4-byte slot per
+// launch, taken round-robin and zeroed on the launch's stream just before it, so launches in
+// flight on different streams use different slots.  Static device memory: nothing is allocated.
+constexpr int kWorkCounterSlots = 4096;
+__device__ unsigned int g_work_counters[kWorkCounterSlots];
+
+namespace {
+unsigned int* g_work_counter_base[kMaxDevices] = {};
+unsigned int g_work_counter_next[kMaxDevices] = {};
+
+int next_work_counter(int dev, unsigned int** out) {
+  std::lock_guard<std::mutex> lk(g_dev.mu);
+  if (g_work_counter_base[dev] == nullptr) {
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_work_counters);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(work counters)");
+    g_work_counter_base[dev] = static_cast<unsigned int*>(ptr);
+  }
+  *out = g_work_counter_base[dev] + (g_work_counter_next[dev]++ % (unsigned)kWorkCounterSlots);
+  return NSA_OK;
+}
+
 int current_sm_count(int* sm_count, int* device) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -415,6 +439,16 @@ int launch(const nsa_sel_desc* d, nsa_stream_t stream) {
       if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
       g_dev.attr_done[dev] |= bit;
     }
+  }
+  p.work_counter = nullptr;
+  const char* env_static = getenv("NSA_SEL_STATIC_UNITS");  // 1: fixed strides (for comparisons)
+  if (pl.n_units > pl.grid && !(env_static != nullptr && atoi(env_static) == 1)) {
+    unsigned int* wc = nullptr;
+    rc = next_work_counter(dev, &wc);
+    if (rc != NSA_OK) return rc;
+    cudaError_t me = cudaMemsetAsync(wc, 0, sizeof(unsigned int), reinterpret_cast<cudaStream_t>(stream));
+    if (me != cudaSuccess) return cuda_fail(me, "cudaMemsetAsync(work counter)");
+    p.work_counter = wc;
   }
   void* args[] = {&tmQ, &tmK, &tmV, &tmO, &p};
   cudaError_t e = cudaLaunchKernel(reinterpret_cast<const void*>(V.kernel), dim3(pl.grid), dim3(V.threads), args,

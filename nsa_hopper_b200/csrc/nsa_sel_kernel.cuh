@@ -95,7 +95,7 @@ struct Ring {
 };
 
 // Info-slot header fields.
-enum : int { kInfNsub = 0, kInfT0, kInfNtok, kInfKend, kInfB, kInfKvh, kInfBkv, kInfSeq0, kInfRef };
+enum : int { kInfNsub = 0, kInfT0, kInfNtok, kInfKend, kInfB, kInfKvh, kInfBkv, kInfSeq0, kInfRef, kInfStop };
 
 struct Params {
   const int32_t* sel;
@@ -115,6 +115,10 @@ struct Params {
   int kv_len, window, key_map;
   int debug_stall;  // 1: the MMA warp first waits on a barrier nothing arrives on (error-path test)
   int out_bufs;     // output staging tiles (2: double buffer; 1 when shared memory is tight)
+  // Work distribution: after the first wave (unit = blockIdx.x), each CTA takes the next unit
+  // from this zeroed global counter, so SMs that run faster take more units; nullptr = fixed
+  // strides of gridDim.x.
+  unsigned int* work_counter;
   int o_accum;             // 1: O += w * result through TMA reduce-add (fp32 O); 0: O = w * result
   const float* o_weight;   // device float w, or nullptr for 1
 };
@@ -220,6 +224,24 @@ __host__ __device__ inline SmemLayout smem_layout(int KS, int VS, int maxsub, in
   return s;
 }
 
+// The bounded part of a wait, out of line: inlined at the ~30 wait sites it made the warp roles'
+// hot loops large enough that instruction fetch stalled them (one copy: north star 11.1 -> 9.8 ms).
+__device__ __noinline__ bool wait_slow(uint64_t* bar, uint32_t parity, int* abort_flag, int32_t* err,
+                                       unsigned long long timeout_ns) {
+  const uint64_t t0 = ptx::globaltimer();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (ptx::mbar_try_wait(bar, parity)) return true;
+    if (*(volatile int*)abort_flag != 0) return false;
+    if (ptx::globaltimer() - t0 > timeout_ns) {
+      *(volatile int*)abort_flag = 1;
+      if (err != nullptr) atomicOr(err, kDevErrTimeout);
+      return false;
+    }
+  }
+}
+
 // A bounded mbarrier wait.  Returns false if the CTA is aborting or the wait ran out of time
 // (then it raises the abort flag and the device error bit).
 struct Waiter {
@@ -233,6 +255,12 @@ struct Waiter {
   }
   __device__ __forceinline__ bool aborted() const { return *(volatile int*)abort_flag != 0; }
   __device__ __forceinline__ bool wait(uint64_t* bar, uint32_t parity) const {
+    if (ptx::mbar_try_wait(bar, parity)) return true;
+    return wait_slow(bar, parity, abort_flag, err, timeout_ns);
+  }
+  // Fully inlined variant, for code whose live registers a call would spill (the wide-tile
+  // softmax holds KPT = 64 scores).
+  __device__ __forceinline__ bool wait_inline(uint64_t* bar, uint32_t parity) const {
     if (ptx::mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = ptx::globaltimer();
     while (true) {
@@ -365,6 +393,7 @@ __device__ int build_unit_info(const Params& p, int u, int* inf, int lane, int i
     inf[kInfBkv] = bkv;
     inf[kInfSeq0] = seq0;
     inf[kInfRef] = bkv * p.NQB + qb;
+    inf[kInfStop] = 0;
   }
   return count;
 }
@@ -380,16 +409,28 @@ __device__ void scheduler_role(const CUtensorMap* tmQ, const Params& p, uint8_t*
   const uint64_t pol_q = ptx::policy_evict_first();
   Ring info, q;
   bool ok = true;
-  int idx = fetch_row_entry(p, blockIdx.x, lane);
-  for (int u = blockIdx.x; u < p.n_units && ok; u += gridDim.x) {
-    const int idx_next = fetch_row_entry(p, u + gridDim.x, lane);  // next row, in flight
+  // The unit after the current one is claimed (and its selection row fetched) one step ahead.
+  auto next_unit = [&](int cur) -> int {
+    if (p.work_counter == nullptr) return cur + (int)gridDim.x;
+    unsigned v = 0;
+    if (lane == 0) v = atomicAdd(p.work_counter, 1u);
+    return (int)gridDim.x + (int)__shfl_sync(0xffffffffu, v, 0);
+  };
+  int u = blockIdx.x;
+  int idx = fetch_row_entry(p, u, lane);
+  int u_next = u < p.n_units ? next_unit(u) : p.n_units;
+  while (u < p.n_units && ok) {
+    const int uc = u;
+    const int idx_next = fetch_row_entry(p, u_next, lane);  // next row, in flight
+    u = u_next;
+    if (u < p.n_units) u_next = next_unit(u);
     if (info.lapped) {
       int r = 1;
       if (lane == 0) r = w.wait(&bars->info_empty[info.idx], info.phase ^ 1u) ? 1 : 0;
       if (!__shfl_sync(0xffffffffu, r, 0)) break;
     }
     int* inf = info_slot(p, smem, info.idx);
-    const int nsub = build_unit_info<C::kExt>(p, u, inf, lane, idx);
+    const int nsub = build_unit_info<C::kExt>(p, uc, inf, lane, idx);
     __syncwarp();
     if (lane == 0) ptx::mbar_arrive(&bars->info_full[info.idx]);
     info.next(kInfoSlots);
@@ -409,6 +450,17 @@ __device__ void scheduler_role(const CUtensorMap* tmQ, const Params& p, uint8_t*
     }
     ok = __shfl_sync(0xffffffffu, r, 0) != 0;
     if (ok) q.next(kQSlots);
+  }
+  // Every consumer leaves its loop at the stop entry that follows the last unit.
+  if (ok) {
+    int r = 1;
+    if (info.lapped && lane == 0) r = w.wait(&bars->info_empty[info.idx], info.phase ^ 1u) ? 1 : 0;
+    if (__shfl_sync(0xffffffffu, r, 0)) {
+      int* inf = info_slot(p, smem, info.idx);
+      if (lane == 0) inf[kInfStop] = 1;
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&bars->info_full[info.idx]);
+    }
   }
   // Drain: the most recent Q load of every slot has landed.
   if (lane == 0) {
@@ -439,11 +491,12 @@ __device__ void kloader_role(const CUtensorMap* tmK, const Params& p, uint8_t* s
   uint8_t* kdst0 = smem + p.off_k + cc * C::kKChunkStride + j * C::kBox;
   Ring info, k;
   bool ok = true;
-  for (int u = blockIdx.x; u < p.n_units && ok; u += gridDim.x) {
+  while (ok) {
     int got = 1;
     if (lane == 0) got = w.wait(&bars->info_full[info.idx], info.phase) ? 1 : 0;
     if (!__shfl_sync(0xffffffffu, got, 0)) break;
     const int* inf = info_slot(p, smem, info.idx);
+    if (inf[kInfStop]) break;
     const int nsub = min(inf[kInfNsub], p.maxsub);
     const int bkv = inf[kInfBkv];
     const int nch = (nsub + 1) >> 1;
@@ -489,11 +542,12 @@ __device__ void vloader_role(const CUtensorMap* tmV, const Params& p, uint8_t* s
   const uint32_t vper = (uint32_t)(p.VS / C::kVGroups);  // V stages per PV warp
   Ring info, v0, v1;  // V stage ring of PV warp 0 / 1
   bool ok = true;
-  for (int u = blockIdx.x; u < p.n_units && ok; u += gridDim.x) {
+  while (ok) {
     int got = 1;
     if (lane == 0) got = w.wait(&bars->info_full[info.idx], info.phase) ? 1 : 0;
     if (!__shfl_sync(0xffffffffu, got, 0)) break;
     const int* inf = info_slot(p, smem, info.idx);
+    if (inf[kInfStop]) break;
     const int nsub = min(inf[kInfNsub], p.maxsub);
     const int bkv = inf[kInfBkv];
     const int nch = (nsub + 1) >> 1;
@@ -554,10 +608,11 @@ __device__ void mma_s_role(const Params& p, uint8_t* smem, SmemBars* bars, const
     uint32_t sc0 = 0, sc1 = 0;  // chunks issued so far for softmax group 0 / 1 (their score buffers)
     const uint32_t k_base = ptx::smem_u32(smem + p.off_k);
     const uint32_t q_base = ptx::smem_u32(smem + p.off_q);
-    for (int u = blockIdx.x; u < p.n_units && ok; u += gridDim.x, ++ui) {
+    for (; ok; ++ui) {
       const int slot = ui % kInfoSlots;
       if (!w.wait(&bars->info_full[slot], (ui / kInfoSlots) & 1)) break;
       const int* inf = info_slot(p, smem, slot);
+      if (inf[kInfStop]) break;
       const int nsub = min(inf[kInfNsub], p.maxsub);
       const int ref = inf[kInfRef];
       const int nch = (nsub + 1) >> 1;
@@ -617,10 +672,11 @@ __device__ void mma_pv_role(const Params& p, uint8_t* smem, SmemBars* bars, cons
     const uint32_t vper = (uint32_t)(p.VS / C::kVGroups);
     const uint32_t v_base = ptx::smem_u32(smem + p.off_v);
     const uint32_t p_base = ptx::smem_u32(smem + p.off_p);
-    for (int u = blockIdx.x; u < p.n_units && ok; u += gridDim.x, ++ui) {
+    for (; ok; ++ui) {
       const int slot = ui % kInfoSlots;
       if (!w.wait(&bars->info_full[slot], (ui / kInfoSlots) & 1)) break;
       const int* inf = info_slot(p, smem, slot);
+      if (inf[kInfStop]) break;
       const int nsub = min(inf[kInfNsub], p.maxsub);
       const int ref = inf[kInfRef];
       const int nch = (nsub + 1) >> 1;
@@ -700,12 +756,17 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, SmemBars* bars, con
   const int col_i = col - (col / p.BQs) * p.BQs;
   uint32_t ui = 0, ne = 0, k = 0;  // k: chunks this group has processed (also its score-buffer ring)
   bool dead = false;
+  auto wt = [&](uint64_t* bar, uint32_t parity) -> bool {
+    if constexpr (NCOL >= 32) return w.wait_inline(bar, parity);
+    else return w.wait(bar, parity);
+  };
 
-  for (int u = blockIdx.x; u < p.n_units; u += gridDim.x, ++ui) {
+  for (;; ++ui) {
     const int slot = ui % kInfoSlots;
-    dead |= !w.wait(&bars->info_full[slot], (ui / kInfoSlots) & 1);
+    dead |= !wt(&bars->info_full[slot], (ui / kInfoSlots) & 1);
     if (ptx::named_bar_or(bar_id, 128, dead)) break;
     const int* inf = info_slot(p, smem, slot);
+    if (inf[kInfStop]) break;
     const int nsub = min(inf[kInfNsub], p.maxsub);
     const int t0 = inf[kInfT0], kend = inf[kInfKend];
     const int nch = (nsub + 1) >> 1;
@@ -728,7 +789,7 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, SmemBars* bars, con
 
     for (int c = wg; c < nch; c += NWG) {
       const int sslot = wg * C::kSPer + (int)(k % (uint32_t)C::kSPer);
-      dead |= !w.wait(&bars->s_full[sslot], (k / (uint32_t)C::kSPer) & 1u);
+      dead |= !wt(&bars->s_full[sslot], (k / (uint32_t)C::kSPer) & 1u);
       ptx::tc_fence_after();
       {
         const uint32_t saddr = tmem + lane_addr + C::kTmemS + sslot * NCOL;
@@ -802,7 +863,7 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, SmemBars* bars, con
       const bool any = ptx::named_bar_or(bar_id, 128, need);
       if (any) {
         // Rescale this group's O^T (lane L = d) once its previous PV (chunk k-1) has landed.
-        dead |= !w.wait(&bars->pv_done[pslot_of<C::kPSlots, NWG>(wg, k - 1)], pphase_of<C::kPSlots, NWG>(k - 1) & 1);
+        dead |= !wt(&bars->pv_done[pslot_of<C::kPSlots, NWG>(wg, k - 1)], pphase_of<C::kPSlots, NWG>(k - 1) & 1);
         ptx::tc_fence_after();
 #pragma unroll
         for (int h0 = 0; h0 < NCOL; h0 += 16) {
@@ -818,7 +879,7 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, SmemBars* bars, con
       // The P buffer was last read by this group's PV of chunk k - NP/NWG.
       const int ps = pslot_of<C::kPSlots, NWG>(wg, k);
       const uint32_t pph = pphase_of<C::kPSlots, NWG>(k);
-      if (pph >= 1) dead |= !w.wait(&bars->pv_done[ps], (pph - 1) & 1);
+      if (pph >= 1) dead |= !wt(&bars->pv_done[ps], (pph - 1) & 1);
 
       const float mref = (m_use == -INFINITY) ? 0.f : m_use;
       float lsum = 0.f;
@@ -856,7 +917,7 @@ __device__ void softmax_role(const Params& p, uint8_t* smem, SmemBars* bars, con
 
     // Publish this group's running max and sum for the epilogue's merge.  The slot of unit
     // ne was last read by the epilogue for unit ne-2 (it arrives on o_empty after that).
-    if (ne >= 2) dead |= !w.wait(&bars->o_empty[ne & 1], ((ne >> 1) - 1) & 1);
+    if (ne >= 2) dead |= !wt(&bars->o_empty[ne & 1], ((ne >> 1) - 1) & 1);
     float lt = l_run;
 #pragma unroll
     for (int o = 1; o < TPC; o <<= 1) lt += __shfl_xor_sync(0xffffffffu, lt, o);
@@ -895,11 +956,12 @@ __device__ void epilogue_role(const CUtensorMap* tmO, const Params& p, uint8_t* 
   uint32_t ui = 0, ne = 0, st = 0;
   bool dead = false;
 
-  for (int u = blockIdx.x; u < p.n_units; u += gridDim.x, ++ui) {
+  for (;; ++ui) {
     const int slot = ui % kInfoSlots;
     dead |= !w.wait(&bars->info_full[slot], (ui / kInfoSlots) & 1);
     if (ptx::named_bar_or(kEpiBar, 128, dead)) break;
     const int* inf = info_slot(p, smem, slot);
+    if (inf[kInfStop]) break;
     const int nsub = min(inf[kInfNsub], p.maxsub);
     const int t0 = inf[kInfT0], ntok = inf[kInfNtok], b = inf[kInfB], kvh = inf[kInfKvh];
     const int nch = (nsub + 1) >> 1;
