@@ -1,0 +1,514 @@
+// Row-owner forward for 128-row query tiles (G heads x 128/G tokens sharing one selection row).
+//
+// Same operation, selection semantics, unit order and loaders as nsa_sel_fwd_kernel (the
+// reference op's per-query-block mode, nsa_v2.cu:42-50, and the NSA window / compressed
+// branches), but with the query rows on the UMMA's M instead of the keys:
+//   S[128 rows x 128 keys] = Q_tile . K_chunk^T      (A = Q, B = K, both K-major SW128)
+//   O[128 rows x d_v]     += P . V_chunk             (A = P in tensor memory, B = V MN-major)
+// so TMEM lane r holds query row r of S, P and O.  The softmax thread that owns row r reads its
+// 128 scores straight from TMEM (no shared-memory transpose, no cross-thread reductions),
+// writes P back over the first 64 columns of the same score buffer as bf16 pairs, and rescales
+// only its own O row when its running max grows.  A tile of 64 rows (the swap-AB kernel's
+// widest) spends most of its time in that transpose; here shared memory carries only the
+// TMA-written K/V/Q tiles, the tensor core's operand reads and the output staging.
+//
+// Warps: 0 K loader, 1 score MMA (owns TMEM), 2-5 epilogue, 6-9 softmax, 10 V loader, 11 PV MMA,
+// 12 scheduler.  TMEM: two score/P buffers of 128 columns, two O buffers of d_v columns.
+// Every ring slot keeps a single in-order consumer per barrier lap, as in nsa_sel_kernel.cuh;
+// the score buffer is released by the PV MMA that read its P (s_empty), which is also what a
+// softmax rescale waits for.
+#pragma once
+#include "nsa_sel_kernel.cuh"
+
+namespace nsa {
+
+template <int DQK_, int DV_, typename OutT_, bool EXT_ = false>
+struct CfgRO {
+  static constexpr int DQK = DQK_, DV = DV_, NCOL = 128, NWG = 1;
+  static constexpr bool kExt = EXT_;
+  using OutT = OutT_;
+  static_assert(DQK == 64 || DQK == 128, "d_qk must be 64 or 128");
+  static_assert(DV == 64 || DV == 128, "d_v must be 64 or 128");
+  static constexpr int kThreads = 13 * 32;
+  static constexpr int kSoftWarp = 6, kVLoadWarp = 10, kPvWarp = 11, kSchedWarp = 12;
+  static constexpr int kBox = kSub * 128;                 // 64 rows x 128 B TMA box (8 KB)
+  static constexpr int kKChunkStride = 2 * kBox;          // one 64-wide d slice of a 128-key K tile
+  static constexpr int kKStage = (DQK / 64) * kKChunkStride;
+  static constexpr int kVSub = (DV / 64) * kBox;          // one 64-key sub-block of V
+  static constexpr int kVStage = 2 * kVSub;
+  static constexpr int kVGroups = 1;
+  static constexpr int kQChunk = 128 * 128;               // one 64-wide d slice of the 128-row Q tile
+  static constexpr int kQBytes = (DQK / 64) * kQChunk;
+  static constexpr int kQS = 1;                           // Q tile ring depth
+  static constexpr int kEPB = 128 / (int)sizeof(OutT);    // O elements per 128-byte box row
+  static constexpr int kOutBoxes = DV / kEPB;             // 128-byte column boxes per O row
+  static constexpr int kOutBox = 128 * 128;               // one staged box: 128 rows x 128 B
+  static constexpr int kStgBoxes = 2;
+  static constexpr int kTmemS = 0;                        // score / P buffers: 2 x 128 columns
+  static constexpr int kTmemO = 256;                      // O accumulators: 2 x DV columns
+  static constexpr int kTmemCols = 512;
+  static constexpr uint32_t kIdescS = ptx::idesc_bf16_f32(128, 128, false, false);
+  static constexpr uint32_t kIdescPV = ptx::idesc_bf16_f32(128, DV, false, true);
+};
+
+template <class C>
+__host__ __device__ inline SmemLayout smem_layout_ro(int KS, int VS, int maxsub, int /*out_bufs*/) {
+  SmemLayout s{};
+  uint32_t o = 0;
+  s.off_k = o; o += (uint32_t)KS * C::kKStage;
+  s.off_v = o; o += (uint32_t)VS * C::kVStage;
+  s.off_q = o; o += (uint32_t)C::kQS * C::kQBytes;
+  o = align_up(o, 1024);
+  s.off_out = o; o += (uint32_t)C::kStgBoxes * C::kOutBox;
+  s.off_ml = o; o += 8u * 2 * 128;  // [unit parity][row] x {m, l}
+  s.off_p = s.off_tr = s.off_alpha = s.off_fac = 0;
+  s.off_info = o; o += 4u * kInfoSlots * (kInfoHdr + maxsub);
+  o = align_up(o, 16);
+  s.off_bar = o; o += (uint32_t)sizeof(SmemBars);
+  s.total = o + 1024;
+  return s;
+}
+
+// ------------------------------------------------------------------------------------------
+// Score MMA: S = Q_tile . K_chunk^T into score buffer kc % 2 once the PV MMA of chunk kc - 2
+// has read that buffer's P.
+// ------------------------------------------------------------------------------------------
+template <class C>
+__device__ void mma_s_role_ro(const Params& p, uint8_t* smem, SmemBars* bars, const Waiter& w, uint32_t tmem,
+                              int lane) {
+  if (lane == 0) {
+    bool ok = true;
+    if (p.debug_stall) ok = w.wait(&bars->stall, 0);
+    uint32_t ui = 0, ne = 0, kc = 0;
+    Ring k;
+    const uint32_t k_base = ptx::smem_u32(smem + p.off_k), q_base = ptx::smem_u32(smem + p.off_q);
+    for (; ok; ++ui) {
+      const int slot = ui % kInfoSlots;
+      if (!w.wait(&bars->info_full[slot], (ui / kInfoSlots) & 1)) break;
+      const int* inf = info_slot(p, smem, slot);
+      if (inf[kInfStop]) break;
+      const int nsub = min(inf[kInfNsub], p.maxsub);
+      const int nch = (nsub + 1) >> 1;
+      if (nch > 0) {
+        const int qs = ne % C::kQS;
+        if (!w.wait(&bars->q_full[qs], (ne / C::kQS) & 1)) break;
+        const uint64_t aq0 = ptx::sdesc_sw128(q_base + qs * C::kQBytes, 16, 1024);
+        for (int c = 0; c < nch; ++c) {
+          const int sl = (int)(kc & 1u);
+          if (kc >= 2 && !w.wait(&bars->s_empty[sl], ((kc >> 1) - 1u) & 1u)) { ok = false; break; }
+          if (!w.wait(&bars->k_full[k.idx], k.phase)) { ok = false; break; }
+          ptx::tc_fence_after();
+          const uint64_t bk0 = ptx::sdesc_sw128(k_base + k.idx * C::kKStage, 16, 1024);
+          const uint32_t dS = tmem + C::kTmemS + sl * 128;
+#pragma unroll
+          for (int j = 0; j < C::DQK / 16; ++j) {
+            const uint32_t ca = (j >> 2) * C::kQChunk + (j & 3) * 32;
+            const uint32_t cb = (j >> 2) * C::kKChunkStride + (j & 3) * 32;
+            ptx::umma_bf16(dS, desc_add(aq0, ca), desc_add(bk0, cb), C::kIdescS, j > 0 ? 1u : 0u);
+          }
+          ptx::umma_commit(&bars->k_empty[k.idx]);
+          ptx::umma_commit(&bars->s_full[sl]);
+          ++kc;
+          k.next((uint32_t)p.KS);
+        }
+        if (!ok) break;
+        ptx::umma_commit(&bars->q_empty[qs]);
+        ++ne;
+      }
+      ptx::mbar_arrive(&bars->info_empty[slot]);
+    }
+    ptx::umma_commit(&bars->drain_s);
+    w.wait_drain(&bars->drain_s, 0);
+  }
+  __syncwarp();
+}
+
+// ------------------------------------------------------------------------------------------
+// PV MMA: O[unit parity] += P (TMEM) . V_chunk; the commit releases the V stage and the score
+// buffer.  Only the sub-blocks that exist are multiplied (a half chunk leaves stale rows of the
+// V stage untouched).
+// ------------------------------------------------------------------------------------------
+template <class C>
+__device__ void mma_pv_role_ro(const Params& p, uint8_t* smem, SmemBars* bars, const Waiter& w, uint32_t tmem,
+                               int lane) {
+  if (lane == 0) {
+    bool ok = true;
+    uint32_t ui = 0, ne = 0, kc = 0;
+    Ring v;
+    const uint32_t v_base = ptx::smem_u32(smem + p.off_v);
+    for (; ok; ++ui) {
+      const int slot = ui % kInfoSlots;
+      if (!w.wait(&bars->info_full[slot], (ui / kInfoSlots) & 1)) break;
+      const int* inf = info_slot(p, smem, slot);
+      if (inf[kInfStop]) break;
+      const int nsub = min(inf[kInfNsub], p.maxsub);
+      const int nch = (nsub + 1) >> 1;
+      if (nch > 0) {
+        // this O buffer (and the unit's ml slot) was last read by the epilogue for unit ne - 2
+        if (ne >= 2 && !w.wait(&bars->o_empty[ne & 1], ((ne >> 1) - 1) & 1)) break;
+        const uint32_t dO = tmem + C::kTmemO + (ne & 1) * C::DV;
+        for (int c = 0; c < nch; ++c) {
+          const int sl = (int)(kc & 1u);
+          const int nsc = min(2, nsub - 2 * c);
+          if (!w.wait(&bars->p_full[sl], (kc >> 1) & 1u)) { ok = false; break; }
+          if (!w.wait(&bars->v_full[v.idx], v.phase)) { ok = false; break; }
+          ptx::tc_fence_after();
+          const uint64_t b0 = ptx::sdesc_sw128(v_base + v.idx * C::kVStage, C::kBox, 1024);
+          const uint32_t aP = tmem + C::kTmemS + sl * 128;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            if (j < nsc * 4) {
+              const uint32_t cb = (j >> 2) * C::kVSub + (j & 3) * 2048;
+              ptx::umma_bf16_ts(dO, aP + j * 8, desc_add(b0, cb), C::kIdescPV, (c == 0 && j == 0) ? 0u : 1u);
+            }
+          }
+          ptx::umma_commit(&bars->v_empty[v.idx]);
+          ptx::umma_commit(&bars->s_empty[sl]);
+          ++kc;
+          v.next((uint32_t)p.VS);
+        }
+        if (!ok) break;
+        ptx::umma_commit(&bars->o_full[ne & 1]);
+        ++ne;
+      }
+      ptx::mbar_arrive(&bars->info_empty[slot]);
+    }
+    ptx::umma_commit(&bars->drain_pv[0]);
+    w.wait_drain(&bars->drain_pv[0], 0);
+  }
+  __syncwarp();
+}
+
+// ------------------------------------------------------------------------------------------
+// Softmax: thread r owns query row r (TMEM lane r) of every chunk.
+// ------------------------------------------------------------------------------------------
+template <class C>
+__device__ __forceinline__ bool ro_key_visible(const Params& p, int key, int s0, int s1, bool has1, int hi,
+                                               int lo, int kend) {
+  const int sb = key >> 6;
+  const int kpos = (sb ? s1 : s0) + (key & 63);
+  if constexpr (C::kExt)
+    return (sb == 0 || has1) && kpos <= hi && kpos >= lo && kpos < kend;
+  else
+    return (sb == 0 || has1) && kpos <= hi && kpos < kend;
+}
+
+template <class C>
+__device__ void softmax_role_ro(const Params& p, uint8_t* smem, SmemBars* bars, const Waiter& w, uint32_t tmem) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int i = threadIdx.x - C::kSoftWarp * 32;     // 0..127 inside the warpgroup
+  const int quarter = warp & 3;
+  const int r = quarter * 32 + lane;                  // the row (TMEM lane) this thread owns
+  const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+  float2* ml = reinterpret_cast<float2*>(smem + p.off_ml);
+  const float sl2 = p.scale_log2;
+  const int ci = r - (r / p.BQs) * p.BQs;            // token of the row inside the unit
+  uint32_t ui = 0, ne = 0, kc = 0;
+  bool dead = false;
+
+  for (;; ++ui) {
+    const int slot = ui % kInfoSlots;
+    dead |= !w.wait_inline(&bars->info_full[slot], (ui / kInfoSlots) & 1);
+    if (ptx::named_bar_or(kWgBar0, 128, dead)) break;
+    const int* inf = info_slot(p, smem, slot);
+    if (inf[kInfStop]) break;
+    const int nsub = min(inf[kInfNsub], p.maxsub);
+    const int t0 = inf[kInfT0], kend = inf[kInfKend];
+    const int nch = (nsub + 1) >> 1;
+    if (nch == 0) {
+      if (i == 0) ptx::mbar_arrive(&bars->info_empty[slot]);
+      continue;
+    }
+    const int t = t0 + ci;
+    int hi = t, lo = INT_MIN / 2, hi_all = t0, lo_all = INT_MIN / 2;
+    if constexpr (C::kExt) {
+      hi = key_hi(p, t);
+      lo = key_lo(p, t);
+      hi_all = key_hi(p, t0);
+      lo_all = key_lo(p, t0 + p.BQs - 1);
+    }
+    const uint32_t obase = tmem + lane_addr + C::kTmemO + (ne & 1) * C::DV;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool first = true;
+
+    for (int c = 0; c < nch; ++c, ++kc) {
+      const int sl = (int)(kc & 1u);
+      dead |= !w.wait_inline(&bars->s_full[sl], (kc >> 1) & 1u);
+      ptx::tc_fence_after();
+      const uint32_t sbase = tmem + lane_addr + C::kTmemS + sl * 128;
+      const int s0 = inf[kInfoHdr + 2 * c];
+      const bool has1 = (2 * c + 1) < nsub;
+      const int s1 = has1 ? inf[kInfoHdr + 2 * c + 1] : 0;
+      bool full = has1 && (max(s0, s1) + kSub - 1 <= hi_all) && (max(s0, s1) + kSub <= kend);
+      if constexpr (C::kExt) full = full && (min(s0, s1) >= lo_all);
+
+      // pass 1: the row's max over the chunk
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        float v[32];
+        ptx::tmem_ld32(sbase + 32 * b, v);
+        ptx::tmem_wait_ld();
+        if (!full) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (!ro_key_visible<C>(p, 32 * b + j, s0, s1, has1, hi, lo, kend)) v[j] = -INFINITY;
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) mx[j & 3] = fmaxf(mx[j & 3], v[j]);
+      }
+      const float cmax_x = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * sl2;
+      float m_use = m_run, alpha = 1.f;
+      if (first) {
+        m_use = cmax_x;
+      } else {
+        const float m_cand = fmaxf(m_run, cmax_x);
+        if (m_cand > m_run + kRescaleLog2) {
+          alpha = (m_run == -INFINITY) ? 0.f : ptx::ex2(m_run - m_cand);
+          m_use = m_cand;
+          // this row's O, once the PV of the previous chunk (which released its buffer) is done
+          dead |= !w.wait_inline(&bars->s_empty[(kc - 1) & 1u], ((kc - 1) >> 1) & 1u);
+          ptx::tc_fence_after();
+#pragma unroll
+          for (int h0 = 0; h0 < C::DV; h0 += 16) {
+            float o[16];
+            ptx::tmem_ld16(obase + h0, o);
+            ptx::tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) o[j] *= alpha;
+            ptx::tmem_st16(obase + h0, o);
+          }
+          ptx::tmem_wait_st();
+        }
+      }
+
+      // pass 2: exp2, row sum, P as bf16 pairs over columns [0, 64) of the same buffer (batch b
+      // reads columns [32b, 32b+32) and writes [16b, 16b+16), all already read)
+      // (mref is finite, so a masked score of -inf gives ex2(-inf) = 0 without a select)
+      const float mref = (m_use == -INFINITY) ? 0.f : m_use;
+      float ls[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        float v[32];
+        ptx::tmem_ld32(sbase + 32 * b, v);
+        ptx::tmem_wait_ld();
+        if (!full) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (!ro_key_visible<C>(p, 32 * b + j, s0, s1, has1, hi, lo, kend)) v[j] = -INFINITY;
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = ptx::ex2(fmaf(v[j], sl2, -mref));
+#pragma unroll
+        for (int j = 0; j < 32; ++j) ls[j & 3] += v[j];
+        uint32_t pk[16];
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) {
+          const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * jj], v[2 * jj + 1]);
+          pk[jj] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        ptx::tmem_st16u(sbase + 16 * b, pk);
+      }
+      ptx::tmem_wait_st();
+      l_run = l_run * alpha + ((ls[0] + ls[1]) + (ls[2] + ls[3]));
+      m_run = m_use;
+      first = false;
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&bars->p_full[sl]);
+    }
+
+    // Publish the row's running max and sum for the epilogue; the ml slot of unit ne was last
+    // read by the epilogue for unit ne - 2.
+    if (ne >= 2) dead |= !w.wait_inline(&bars->o_empty[ne & 1], ((ne >> 1) - 1) & 1);
+    ml[(ne & 1) * 128 + r] = make_float2(m_run, l_run);
+    __syncwarp();
+    if (lane == 0) ptx::mbar_arrive(&bars->wg_done[ne & 1]);
+    if (i == 0) ptx::mbar_arrive(&bars->info_empty[slot]);
+    ++ne;
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// Epilogue: thread r scales O row r by w / l, writes the LSE, and stages the row into 128-byte
+// boxes (SW128 layout: 16-byte chunk j of row r at j ^ (r & 7)) that TMA stores, or adds with a
+// TMA reduce when the descriptor asks to accumulate.
+// ------------------------------------------------------------------------------------------
+template <class C>
+__device__ void epilogue_role_ro(const CUtensorMap* tmO, const Params& p, uint8_t* smem, SmemBars* bars,
+                                 const Waiter& w, uint32_t tmem) {
+  using OutT = typename C::OutT;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int i = threadIdx.x - kEpiWarp0 * 32;
+  const int quarter = warp & 3;
+  const int r = quarter * 32 + lane;
+  const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+  const float2* ml = reinterpret_cast<const float2*>(smem + p.off_ml);
+  uint8_t* stg = smem + p.off_out;
+  const float wgt = p.o_weight != nullptr ? __ldg(p.o_weight) : 1.f;
+  const int cg = r / p.BQs, ci = r - (r / p.BQs) * p.BQs;
+  uint32_t ui = 0, ne = 0, nbox = 0;
+  bool dead = false;
+
+  for (;; ++ui) {
+    const int slot = ui % kInfoSlots;
+    dead |= !w.wait(&bars->info_full[slot], (ui / kInfoSlots) & 1);
+    if (ptx::named_bar_or(kEpiBar, 128, dead)) break;
+    const int* inf = info_slot(p, smem, slot);
+    if (inf[kInfStop]) break;
+    const int nsub = min(inf[kInfNsub], p.maxsub);
+    const int t0 = inf[kInfT0], ntok = inf[kInfNtok], b = inf[kInfB], kvh = inf[kInfKvh];
+    const int nch = (nsub + 1) >> 1;
+    if (nch > 0) {
+      dead |= !w.wait(&bars->wg_done[ne & 1], (ne >> 1) & 1);
+      dead |= !w.wait(&bars->o_full[ne & 1], (ne >> 1) & 1);
+      ptx::tc_fence_after();
+    }
+    const float2 v_ml = nch > 0 ? ml[(ne & 1) * 128 + r] : make_float2(-INFINITY, 0.f);
+    const float scale = v_ml.y > 0.f ? wgt / v_ml.y : 0.f;
+    if (ci < ntok && p.lse != nullptr) {
+      const float lse = v_ml.y > 0.f ? (v_ml.x + log2f(v_ml.y)) * 0.69314718055994530942f : -INFINITY;
+      p.lse[((size_t)b * p.Hq + (size_t)kvh * p.G + cg) * p.T + t0 + ci] = lse;
+    }
+    if (ntok > 0) {
+      const uint32_t obase = tmem + lane_addr + C::kTmemO + (ne & 1) * C::DV;
+      for (int bx = 0; bx < C::kOutBoxes; ++bx, ++nbox) {
+        uint8_t* box = stg + (nbox % C::kStgBoxes) * C::kOutBox;
+        if (i == 0) ptx::bulk_wait_read<C::kStgBoxes - 1>();  // the box's previous store has read it
+        ptx::named_bar_sync(kEpiBar, 128);
+        float v[C::kEPB];
+#pragma unroll
+        for (int h0 = 0; h0 < C::kEPB; h0 += 16) {
+          if (nch > 0) {
+            ptx::tmem_ld16(obase + bx * C::kEPB + h0, *reinterpret_cast<float(*)[16]>(&v[h0]));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[h0 + j] = 0.f;
+          }
+        }
+        if (nch > 0) ptx::tmem_wait_ld();
+        uint8_t* row = box + r * 128;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          uint4 q;
+          if constexpr (sizeof(OutT) == 4) {
+            q.x = __float_as_uint(v[4 * j + 0] * scale);
+            q.y = __float_as_uint(v[4 * j + 1] * scale);
+            q.z = __float_as_uint(v[4 * j + 2] * scale);
+            q.w = __float_as_uint(v[4 * j + 3] * scale);
+          } else {
+            __nv_bfloat162 h0 = __floats2bfloat162_rn(v[8 * j + 0] * scale, v[8 * j + 1] * scale);
+            __nv_bfloat162 h1 = __floats2bfloat162_rn(v[8 * j + 2] * scale, v[8 * j + 3] * scale);
+            __nv_bfloat162 h2 = __floats2bfloat162_rn(v[8 * j + 4] * scale, v[8 * j + 5] * scale);
+            __nv_bfloat162 h3 = __floats2bfloat162_rn(v[8 * j + 6] * scale, v[8 * j + 7] * scale);
+            q.x = *reinterpret_cast<const uint32_t*>(&h0);
+            q.y = *reinterpret_cast<const uint32_t*>(&h1);
+            q.z = *reinterpret_cast<const uint32_t*>(&h2);
+            q.w = *reinterpret_cast<const uint32_t*>(&h3);
+          }
+          *reinterpret_cast<uint4*>(row + ((j ^ (r & 7)) << 4)) = q;
+        }
+        ptx::fence_proxy_async_smem();
+        ptx::named_bar_sync(kEpiBar, 128);
+        if (i == 0) {
+          if (p.o_accum)
+            ptx::tma_reduce_add_4d(tmO, box, bx * C::kEPB, t0, kvh * p.G, b);
+          else
+            ptx::tma_store_4d(tmO, box, bx * C::kEPB, t0, kvh * p.G, b);
+          ptx::bulk_commit();
+        }
+      }
+    }
+    if (nch > 0) {
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&bars->o_empty[ne & 1]);  // O buffer and ml slot are free
+      ++ne;
+    }
+    if (i == 0) ptx::mbar_arrive(&bars->info_empty[slot]);
+  }
+  if (i == 0) ptx::bulk_wait<0>();
+}
+
+// ------------------------------------------------------------------------------------------
+template <class C>
+__global__ void __launch_bounds__(C::kThreads, 1)
+    nsa_ro_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                      const __grid_constant__ Params p) {
+  uint8_t* smem = smem_base();
+  SmemBars* bars = reinterpret_cast<SmemBars*>(smem + p.off_bar);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kInfoSlots; ++s) {
+      ptx::mbar_init(&bars->info_full[s], 1);
+      // consumers: K and V loaders, score MMA, PV MMA, softmax, epilogue
+      ptx::mbar_init(&bars->info_empty[s], 6);
+    }
+    for (int s = 0; s < 2; ++s) {
+      ptx::mbar_init(&bars->s_full[s], 1);   // score MMA commit
+      ptx::mbar_init(&bars->s_empty[s], 1);  // PV MMA commit: P read, buffer free
+      ptx::mbar_init(&bars->p_full[s], 4);   // softmax warps
+      ptx::mbar_init(&bars->o_full[s], 1);
+      ptx::mbar_init(&bars->wg_done[s], 4);
+      ptx::mbar_init(&bars->o_empty[s], 4);
+    }
+    for (int s = 0; s < kQSlots; ++s) {
+      ptx::mbar_init(&bars->q_full[s], 1);
+      ptx::mbar_init(&bars->q_empty[s], 1);
+    }
+    for (int s = 0; s < kMaxStages; ++s) {
+      ptx::mbar_init(&bars->k_full[s], 1);
+      ptx::mbar_init(&bars->k_empty[s], 1);
+      ptx::mbar_init(&bars->v_full[s], 1);
+      ptx::mbar_init(&bars->v_empty[s], 1);
+    }
+    ptx::mbar_init(&bars->drain_s, 1);
+    ptx::mbar_init(&bars->drain_pv[0], 1);
+    ptx::mbar_init(&bars->drain_pv[1], 1);
+    ptx::mbar_init(&bars->stall, 1);
+    bars->abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == kLoaderWarp && lane == 0) {
+    ptx::prefetch_tmap(&tmQ);
+    ptx::prefetch_tmap(&tmK);
+    ptx::prefetch_tmap(&tmV);
+    ptx::prefetch_tmap(&tmO);
+  }
+  if (warp == kMmaWarp) {
+    ptx::tmem_alloc(&bars->tmem_base, C::kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+  const Waiter w{&bars->abort_flag, p.err, p.timeout_ns};
+
+  if (warp == kLoaderWarp) {
+    kloader_role<C>(&tmK, p, smem, bars, w, lane);
+  } else if (warp == kMmaWarp) {
+    mma_s_role_ro<C>(p, smem, bars, w, tmem, lane);
+  } else if (warp < C::kSoftWarp) {
+    epilogue_role_ro<C>(&tmO, p, smem, bars, w, tmem);
+  } else if (warp < C::kVLoadWarp) {
+    softmax_role_ro<C>(p, smem, bars, w, tmem);
+  } else if (warp == C::kVLoadWarp) {
+    vloader_role<C>(&tmV, p, smem, bars, w, lane);
+  } else if (warp == C::kPvWarp) {
+    mma_pv_role_ro<C>(p, smem, bars, w, tmem, lane);
+  } else {
+    scheduler_role<C>(&tmQ, p, smem, bars, w, lane);
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
+}  // namespace nsa

@@ -19,6 +19,7 @@
 
 #include "nsa_sel.h"
 #include "nsa_sel_kernel.cuh"
+#include "nsa_ro_kernel.cuh"
 #include "nsa_select_kernel.cuh"
 
 namespace {
@@ -124,6 +125,7 @@ struct Variant {
   KernelFn kernel;
   LayoutFn layout;
   int k_stage, v_stage, tmem_cols;
+  int ro;  // row-owner kernel (128-row query tiles, nsa_ro_kernel.cuh)
 };
 
 template <int DQK, int DV, int NCOL, typename OutT, int NWG, bool EXT = false>
@@ -141,7 +143,27 @@ Variant make_variant() {
                  &nsa::smem_layout<C>,
                  C::kKStage,
                  C::kVStage,
-                 C::kTmemCols};
+                 C::kTmemCols,
+                 0};
+}
+
+template <int DQK, int DV, typename OutT, bool EXT = false>
+Variant make_variant_ro() {
+  using C = nsa::CfgRO<DQK, DV, OutT, EXT>;
+  return Variant{DQK,
+                 DV,
+                 128,
+                 sizeof(OutT) == 4 ? 1 : 0,
+                 1,
+                 EXT ? 1 : 0,
+                 1,
+                 C::kThreads,
+                 reinterpret_cast<KernelFn>(&nsa::nsa_ro_fwd_kernel<C>),
+                 &nsa::smem_layout_ro<C>,
+                 C::kKStage,
+                 C::kVStage,
+                 C::kTmemCols,
+                 1};
 }
 
 // Narrow tiles (N = 16: per-token selection with G <= 16) split every unit's chunks over two
@@ -159,7 +181,11 @@ Variant make_variant() {
 
 const Variant* variants(int* n) {
   static const Variant v[] = {NSA_VARIANTS_FOR(64, 64),  NSA_VARIANTS_FOR(128, 128), NSA_VARIANTS_FOR(192, 128),
-                              NSA_VARIANTS_FOR(128, 64), NSA_EXT_VARIANTS_FOR(64),   NSA_EXT_VARIANTS_FOR(128)};
+                              NSA_VARIANTS_FOR(128, 64), NSA_EXT_VARIANTS_FOR(64),   NSA_EXT_VARIANTS_FOR(128),
+                              // 128-row query tiles (G * tokens per unit = 128): row-owner kernel
+                              make_variant_ro<64, 64, bf16>(), make_variant_ro<64, 64, float>(),
+                              make_variant_ro<128, 128, bf16>(), make_variant_ro<128, 128, float>(),
+                              make_variant_ro<64, 64, float, true>(), make_variant_ro<128, 128, float, true>()};
   *n = (int)(sizeof(v) / sizeof(v[0]));
   return v;
 }
@@ -193,7 +219,8 @@ int make_plan(const nsa_sel_desc* d, int sm_count, Plan* pl) {
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || T <= 0) return fail(NSA_ERR_INVALID_ARG, "B, Hq, Hkv, T must be positive");
   if (Hq % Hkv != 0) return fail(NSA_ERR_INVALID_ARG, "Hq (%d) must be a multiple of Hkv (%d)", Hq, Hkv);
   const int G = Hq / Hkv;
-  if (G > kMaxCols) return fail(NSA_ERR_UNSUPPORTED, "group size G=%d exceeds %d", G, kMaxCols);
+  if (G > 128 || (G > kMaxCols && 128 % G != 0))
+    return fail(NSA_ERR_UNSUPPORTED, "group size G=%d exceeds %d", G, kMaxCols);
   if (d->d_qk <= 0 || d->d_v <= 0) return fail(NSA_ERR_INVALID_ARG, "d_qk and d_v must be positive");
   if (d->block_size <= 0) return fail(NSA_ERR_INVALID_ARG, "l_prime must be positive");
   if (d->block_size % 64 != 0 || d->block_size > 256)
@@ -234,15 +261,28 @@ int make_plan(const nsa_sel_desc* d, int sm_count, Plan* pl) {
       (long long)T * d->d_qk >= (1ll << 31) || (long long)B * Hkv * NQB * d->n_sel >= (1ll << 31))
     return fail(NSA_ERR_UNSUPPORTED, "problem too large for 32-bit coordinates");
 
-  // Tokens per work unit: the largest divisor of BQ with G * tokens <= 128.
-  int bqs = 1;
-  for (int c = d->q_block; c >= 1; --c)
-    if (d->q_block % c == 0 && G * c <= kMaxCols) { bqs = c; break; }
-  const int rows = G * bqs;
-  int ncol = 16;
-  while (ncol < rows) ncol <<= 1;
+  // Tokens per work unit.  When 128 query rows (G heads x 128/G tokens) fit one selection row,
+  // the row-owner kernel takes the unit (queries on the MMA's M); otherwise the largest divisor
+  // of BQ with G * tokens <= 64 goes to the swap-AB kernel (keys on M).
   const int ext = (d->window > 0 || d->key_map != NSA_KEYMAP_CAUSAL) ? 1 : 0;
-  const int vi = find_variant(d->d_qk, d->d_v, ncol, d->o_dtype == NSA_DTYPE_F32 ? 1 : 0, ext);
+  const int of32 = d->o_dtype == NSA_DTYPE_F32 ? 1 : 0;
+  const char* env_ro = getenv("NSA_SEL_NO_RO");  // 1: never use the row-owner kernel (comparisons)
+  int bqs = 1, ncol = 16, vi = -1;
+  if (!(env_ro != nullptr && atoi(env_ro) == 1) && d->cyc == nullptr && 128 % G == 0 && d->q_block % (128 / G) == 0) {
+    vi = find_variant(d->d_qk, d->d_v, 128, of32, ext);
+    if (vi >= 0) {
+      bqs = 128 / G;
+      ncol = 128;
+    }
+  }
+  if (vi < 0 && G > kMaxCols) return fail(NSA_ERR_UNSUPPORTED, "group size G=%d exceeds %d", G, kMaxCols);
+  if (vi < 0) {
+    for (int c = d->q_block; c >= 1; --c)
+      if (d->q_block % c == 0 && G * c <= kMaxCols) { bqs = c; break; }
+    const int rows = G * bqs;
+    while (ncol < rows) ncol <<= 1;
+    vi = find_variant(d->d_qk, d->d_v, ncol, of32, ext);
+  }
   if (vi < 0)
     return fail(NSA_ERR_UNSUPPORTED,
                 ext ? "no kernel with window / key map for (d_qk=%d, d_v=%d, %s O); built: d_qk == d_v in {64, 128}, fp32 O"
@@ -367,9 +407,11 @@ int launch(const nsa_sel_desc* d, nsa_stream_t stream) {
     const cuuint64_t es = f32 ? 4 : 2;
     cuuint64_t dims[4] = {dv, (cuuint64_t)T, (cuuint64_t)Hq, (cuuint64_t)B};
     cuuint64_t str[3] = {dv * es, dv * es * T, dv * es * T * Hq};
-    cuuint32_t box[4] = {64, (cuuint32_t)pl.BQs, (cuuint32_t)pl.G, 1};
+    // row-owner kernel: 128-byte-wide boxes staged in the SW128 layout; swap-AB kernel: 64-column
+    // unswizzled boxes
+    cuuint32_t box[4] = {V.ro ? (cuuint32_t)(128 / es) : 64u, (cuuint32_t)pl.BQs, (cuuint32_t)pl.G, 1};
     rc = encode(&tmO, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, d->o, dims, str,
-                box, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, "O");
+                box, V.ro ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, "O");
     if (rc != NSA_OK) return rc;
   }
 

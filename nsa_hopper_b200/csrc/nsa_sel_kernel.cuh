@@ -195,6 +195,7 @@ struct Cfg {
   static_assert(kSSlots <= kMaxSSlots && kSSlots % NWG == 0, "score buffers");
   static constexpr uint32_t kIdescS = ptx::idesc_bf16_f32(128, NCOL, false, false);
   static constexpr uint32_t kIdescPV = ptx::idesc_bf16_f32(128, NCOL, true, false);
+  static constexpr int kQS = kQSlots;  // Q tile ring depth
 };
 
 // Shared-memory layout (byte offsets from a 1024-aligned base); identical on host and device.
@@ -207,7 +208,7 @@ __host__ __device__ inline SmemLayout smem_layout(int KS, int VS, int maxsub, in
   uint32_t o = 0;
   s.off_k = o; o += (uint32_t)KS * C::kKStage;
   s.off_v = o; o += (uint32_t)VS * C::kVStage;
-  s.off_q = o; o += (uint32_t)kQSlots * C::kQBytes;
+  s.off_q = o; o += (uint32_t)C::kQS * C::kQBytes;
   o = align_up(o, 1024);
   s.off_p = o; o += (uint32_t)C::kPSlots * C::kPBytes;
   o = align_up(o, 128);
@@ -449,7 +450,7 @@ __device__ void scheduler_role(const CUtensorMap* tmQ, const Params& p, uint8_t*
       }
     }
     ok = __shfl_sync(0xffffffffu, r, 0) != 0;
-    if (ok) q.next(kQSlots);
+    if (ok) q.next(C::kQS);
   }
   // Every consumer leaves its loop at the stop entry that follows the last unit.
   if (ok) {
@@ -465,10 +466,10 @@ __device__ void scheduler_role(const CUtensorMap* tmQ, const Params& p, uint8_t*
   // Drain: the most recent Q load of every slot has landed.
   if (lane == 0) {
     Ring d = q;
-    for (int s2 = 0; s2 < kQSlots; ++s2) {
-      // slot d.idx - 1 - s2 (mod kQSlots), lap parity adjusted when it wraps
+    for (int s2 = 0; s2 < C::kQS; ++s2) {
+      // slot d.idx - 1 - s2 (mod kQS), lap parity adjusted when it wraps
       const uint32_t back = (uint32_t)s2 + 1u;
-      const uint32_t slot = (d.idx + kQSlots - back % kQSlots) % kQSlots;
+      const uint32_t slot = (d.idx + C::kQS - back % C::kQS) % C::kQS;
       const uint32_t ph = (d.idx >= back) ? d.phase : (d.phase ^ 1u);
       if (d.lapped || d.idx >= back) w.wait_drain(&bars->q_full[slot], ph);
     }
@@ -617,9 +618,9 @@ __device__ void mma_s_role(const Params& p, uint8_t* smem, SmemBars* bars, const
       const int ref = inf[kInfRef];
       const int nch = (nsub + 1) >> 1;
       if (nch > 0) {
-        const int qs = ne % kQSlots;
+        const int qs = ne % C::kQS;
         long long t_wait = 0;
-        if (!w.wait(&bars->q_full[qs], (ne / kQSlots) & 1)) break;
+        if (!w.wait(&bars->q_full[qs], (ne / C::kQS) & 1)) break;
         const uint64_t bq0 = ptx::sdesc_sw128(q_base + qs * C::kQBytes, 16, 1024);
         for (int c = 0; c < nch; ++c, k.next((uint32_t)p.KS)) {
           const bool g1 = C::NWG == 2 && (c & 1);
@@ -1102,7 +1103,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     ptx::fence_mbar_init();
   }
   // Rows of the Q tiles beyond G*BQs are never written by TMA and must read as zero.
-  for (int idx = threadIdx.x; idx < kQSlots * C::kQBytes / 16; idx += C::kThreads)
+  for (int idx = threadIdx.x; idx < C::kQS * C::kQBytes / 16; idx += C::kThreads)
     reinterpret_cast<uint4*>(smem + p.off_q)[idx] = make_uint4(0u, 0u, 0u, 0u);
   ptx::fence_proxy_async_smem();
   if (warp == kLoaderWarp && lane == 0) {

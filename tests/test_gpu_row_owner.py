@@ -1,0 +1,114 @@
+"""The row-owner kernel (nsa_ro_kernel.cuh: 128 query rows per unit on the MMA's M, P in tensor
+memory) against the oracle, on the shapes that route to it: G * BQ covering whole 128-row tiles
+(128 % G == 0 and BQ % (128 / G) == 0)."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from nsa_hopper_b200 import capi, indices, nsa, ops
+from tests.helpers import compare, make_qkv, run_capi
+
+pytestmark = pytest.mark.gpu
+
+
+def _routes_to_row_owner(Hq, Hkv, BQ):
+    G = Hq // Hkv
+    return 128 % G == 0 and BQ % (128 // G) == 0
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,S,D,KSEL,BQ,lp,f32", [
+    (1, 16, 1, 1000, 64, 6, 8, 64, True),       # G = 16, 8 tokens per tile, T not a multiple of 64
+    (2, 64, 4, 1024, 128, 16, 8, 64, False),    # the north-star head layout, bf16 O
+    (1, 32, 4, 1111, 128, 8, 16, 128, True),    # G = 8, l' = 128
+    (1, 128, 1, 300, 64, 4, 1, 64, False),      # G = 128: one token per tile
+    (1, 64, 2, 777, 64, 5, 4, 256, True),       # G = 32, l' = 256
+    (1, 1, 1, 700, 128, 4, 128, 64, False),     # G = 1: 128 tokens share a row
+    (1, 16, 1, 768, 64, 6, 16, 64, True),       # BQ = 16: two tiles per query block
+])
+def test_row_owner_matches_oracle(B, Hq, Hkv, S, D, KSEL, BQ, lp, f32):
+    assert _routes_to_row_owner(Hq, Hkv, BQ)
+    q, k, v = make_qkv(B, Hq, Hkv, S, D, D, seed=S + KSEL)
+    sel = indices.perm_qblock(B, Hkv, S, KSEL, BQ, lp, seed=S, heads_share=False)
+    o, lse = run_capi(q, k, v, torch.from_numpy(sel), BQ=BQ, l_prime=lp, out_f32=f32)
+    torch.cuda.synchronize()
+    o_ref, lse_ref = oracle.forward(q, k, v, sel, lp, BQ)
+    compare(o, lse, o_ref, lse_ref)
+
+
+def test_row_owner_plan():
+    d = capi.make_desc(q=256, k=256, v=256, sel=256, o=256, batch=1, heads_q=64, heads_kv=4, seq_len=4096, d_qk=128,
+                       d_v=128, n_qblocks=512, n_sel=16, block_size=64, q_block=8, o_dtype=capi.DTYPE_BF16)
+    p = capi.plan(d)
+    assert p["n_cols"] == 128 and p["q_per_unit"] == 8 and p["tmem_cols"] == 512
+
+
+def test_row_owner_edge_selection_rows():
+    """-1 padding, duplicates, the scratch id, ids past the end and future blocks, per query block."""
+    B, Hq, Hkv, T, D, n, BQ = 1, 16, 2, 900, 64, 6, 16
+    q, k, v = make_qkv(B, Hq, Hkv, T, D, D, seed=15)
+    rng = np.random.default_rng(15)
+    nblk = (T + 63) // 64
+    NQB = (T + BQ - 1) // BQ
+    sel = rng.integers(-3, nblk + 3, size=(B, Hkv, NQB, n)).astype(np.int32)
+    sel[:, :, ::7, :] = -1
+    sel[:, :, 3::11, 1] = sel[:, :, 3::11, 0]
+    sel[:, 0, 5::13, :] = nblk
+    o, lse = run_capi(q, k, v, torch.from_numpy(sel), BQ=BQ, out_f32=True)
+    torch.cuda.synchronize()
+    o_ref, lse_ref = oracle.forward(q, k, v, sel, 64, BQ)
+    compare(o, lse, o_ref, lse_ref)
+
+
+def test_row_owner_mask_probe_counts_exact():
+    """Q = 0: exp(LSE) is the exact number of visible keys of every row (tile rows, causal edge,
+    ragged end)."""
+    B, Hq, Hkv, T, D, n, BQ = 1, 16, 2, 1100, 128, 16, 8
+    _, k, _ = make_qkv(B, Hq, Hkv, T, D, D, seed=16)
+    q = torch.zeros(B, Hq, T, D, dtype=torch.bfloat16)
+    v = torch.zeros(B, Hkv, T, D, dtype=torch.bfloat16)
+    sel = indices.perm_qblock(B, Hkv, T, n, BQ, 64, seed=16, heads_share=False)
+    o, lse = run_capi(q, k, v, torch.from_numpy(sel), BQ=BQ, out_f32=True)
+    torch.cuda.synchronize()
+    counts = oracle.count_keys(sel, T, 64, BQ).reshape(B, Hkv, T)
+    cnt = np.repeat(counts, Hq // Hkv, axis=1).astype(np.float64)
+    got = np.exp(lse.cpu().numpy().astype(np.float64))
+    assert np.array_equal(np.rint(got), cnt)
+
+
+@pytest.mark.parametrize("T,window,D", [(1500, 128, 64), (2048, 512, 128), (777, 100, 128)])
+def test_row_owner_window_branch(T, window, D):
+    B, Hq, Hkv = 1, 32, 2
+    g = torch.Generator(device="cuda").manual_seed(T)
+    q = torch.randn(B, Hq, T, D, device="cuda", generator=g).to(torch.bfloat16)
+    k = torch.randn(B, Hkv, T, D, device="cuda", generator=g).to(torch.bfloat16)
+    v = torch.randn(B, Hkv, T, D, device="cuda", generator=g).to(torch.bfloat16)
+    bq = 128 // (Hq // Hkv)
+    sel = nsa.window_selection(B, Hkv, T, window, 64, q.device, bq)
+    o, lse = ops.forward_ext(q, k, v, sel, 64, bq, window=window)
+    ref = nsa.window_branch(q, k, v, window)
+    torch.cuda.synchronize()
+    assert (o - ref).abs().max().item() <= 2e-2
+
+
+@pytest.mark.parametrize("T,D", [(1500, 64), (4096, 128), (40, 64)])
+def test_row_owner_compressed_branch_accumulates(T, D):
+    """Compressed key map on the row-owner kernel, written with a weight and then added into an
+    existing O (TMA reduce-add from the swizzled staging boxes)."""
+    B, Hq, Hkv = 1, 16, 1
+    g = torch.Generator(device="cuda").manual_seed(3 * T)
+    q = torch.randn(B, Hq, T, D, device="cuda", generator=g).to(torch.bfloat16)
+    k = torch.randn(B, Hkv, T, D, device="cuda", generator=g).to(torch.bfloat16)
+    v = torch.randn(B, Hkv, T, D, device="cuda", generator=g).to(torch.bfloat16)
+    Kc, Vc = nsa.compress_kv(k, v, 32, 16)
+    if Kc.shape[2] == 0:
+        pytest.skip("no compressed keys")
+    Kc, Vc = Kc.to(torch.bfloat16).contiguous(), Vc.to(torch.bfloat16).contiguous()
+    bq = 128 // (Hq // Hkv)
+    sel = nsa.compressed_selection(B, Hkv, T, Kc.shape[2], q.device, bq)
+    ref = nsa.compressed_branch(q, Kc.float(), Vc.float())
+    w = torch.tensor([0.25], device="cuda")
+    base = torch.randn(B, Hq, T, D, device="cuda", generator=g)
+    o, _ = ops.forward_ext(q, Kc, Vc, sel, 64, bq, key_map=1, out=base.clone(), weight=w, accumulate=True)
+    torch.cuda.synchronize()
+    assert (o - (base + 0.25 * ref)).abs().max().item() <= 1e-2
