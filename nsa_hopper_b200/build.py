@@ -48,7 +48,9 @@ def _run(cmd: List[str]) -> None:
 
 
 def build_kernel_lib(force: bool = False, extra: List[str] = ()) -> str:
-    srcs = [os.path.join(CSRC, f) for f in ("nsa_sel_api.cu", "nsa_sel_kernel.cuh", "nsa_select_kernel.cuh", "nsa_linspace.cuh", "ptx.cuh")]
+    # the translation unit first, then every header it may include (staleness check)
+    srcs = [os.path.join(CSRC, "nsa_sel_api.cu")] + sorted(
+        os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith(".cuh"))
     srcs.append(os.path.join(INCLUDE, "nsa_sel.h"))
     if not force and not _stale(LIB, srcs):
         return LIB

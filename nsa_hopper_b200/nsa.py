@@ -135,9 +135,13 @@ def select_blocks(Q: torch.Tensor, Kc: torch.Tensor, n_sel: int, l_prime: int, c
 def branch_q_block(G: int) -> int:
     """Query tokens per selection row for the window and compressed branches: every token of a
     query block shares its row (the union of the tokens' blocks; the kernel masks each token
-    exactly), and BQ = 64 / G fills the kernel's 64-column tile (G heads x BQ tokens), so one
-    score MMA serves BQ tokens.  Measured at B=1, T=65536, Hq=64, Hkv=4, d=128 on a B200: window
-    14.4 -> 6.2 ms, compressed 27.9 -> 16.2 ms against BQ = 1."""
+    exactly).  BQ = 128 / G fills a 128-row query tile of the row-owner kernel (G heads x BQ
+    tokens on the MMA's M); a G that does not divide 128 gets the largest power of two with
+    G * BQ <= 64 for the swap-AB kernel.  Measured at B=1, T=65536, Hq=64, Hkv=4, d=128 on a
+    B200 (window 512, 32/16 compression): window 14.4 ms (BQ=1) / 7.1 (BQ=4) / 3.7 (BQ=8,
+    row owner); compressed 27.9 / 17.7 / 7.4 ms."""
+    if G <= 128 and 128 % G == 0:
+        return 128 // G
     bq = 1
     while G * bq * 2 <= 64:
         bq *= 2

@@ -168,5 +168,6 @@ def test_window_selection_rows_cover_exactly_the_window(T, window, bq):
         assert row[:len(want)] == want and all(x == -1 for x in row[len(want):])
 
 
-def test_branch_q_block_fills_the_64_column_tile():
-    assert [nsa.branch_q_block(g) for g in (1, 4, 8, 16, 32, 64, 128)] == [64, 16, 8, 4, 2, 1, 1]
+def test_branch_q_block_fills_the_query_tile():
+    assert [nsa.branch_q_block(g) for g in (1, 4, 8, 16, 32, 64, 128)] == [128, 32, 16, 8, 4, 2, 1]
+    assert [nsa.branch_q_block(g) for g in (3, 12, 24, 48)] == [16, 4, 2, 1]
