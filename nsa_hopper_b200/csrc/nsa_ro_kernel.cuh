@@ -12,8 +12,9 @@
 // widest) spends most of its time in that transpose; here shared memory carries only the
 // TMA-written K/V/Q tiles, the tensor core's operand reads and the output staging.
 //
-// Warps: 0 K loader, 1 score MMA (owns TMEM), 2-5 epilogue, 6-9 softmax, 10 V loader, 11 PV MMA,
-// 12 scheduler.  TMEM: two score/P buffers of 128 columns, two O buffers of d_v columns.
+// Warps: 0 K loader, 1 score MMA (owns TMEM), 2-5 epilogue, 6-13 softmax (two warpgroups: keys 0-63
+// and 64-127 of every chunk), 14 V loader, 15 PV MMA, 16 scheduler.  TMEM: two score/P buffers of
+// 128 columns, two O buffers of d_v columns.
 // Every ring slot keeps a single in-order consumer per barrier lap, as in nsa_sel_kernel.cuh;
 // the score buffer is released by the PV MMA that read its P (s_empty), which is also what a
 // softmax rescale waits for.
@@ -29,8 +30,8 @@ struct CfgRO {
   using OutT = OutT_;
   static_assert(DQK == 64 || DQK == 128, "d_qk must be 64 or 128");
   static_assert(DV == 64 || DV == 128, "d_v must be 64 or 128");
-  static constexpr int kThreads = 13 * 32;
-  static constexpr int kSoftWarp = 6, kVLoadWarp = 10, kPvWarp = 11, kSchedWarp = 12;
+  static constexpr int kThreads = 17 * 32;
+  static constexpr int kSoftWarp = 6, kVLoadWarp = 14, kPvWarp = 15, kSchedWarp = 16;
   static constexpr int kBox = kSub * 128;                 // 64 rows x 128 B TMA box (8 KB)
   static constexpr int kKChunkStride = 2 * kBox;          // one 64-wide d slice of a 128-key K tile
   static constexpr int kKStage = (DQK / 64) * kKChunkStride;
@@ -61,7 +62,9 @@ __host__ __device__ inline SmemLayout smem_layout_ro(int KS, int VS, int maxsub,
   o = align_up(o, 1024);
   s.off_out = o; o += (uint32_t)C::kStgBoxes * C::kOutBox;
   s.off_ml = o; o += 8u * 2 * 128;  // [unit parity][row] x {m, l}
-  s.off_p = s.off_tr = s.off_alpha = s.off_fac = 0;
+  s.off_alpha = o; o += 4u * 2 * 2 * 128;  // softmax exchange: [chunk parity][half][row] partial max
+  s.off_fac = o; o += 4u * 128;            // softmax exchange: second half's row sum
+  s.off_p = s.off_tr = 0;
   s.off_info = o; o += 4u * kInfoSlots * (kInfoHdr + maxsub);
   o = align_up(o, 16);
   s.off_bar = o; o += (uint32_t)sizeof(SmemBars);
@@ -154,12 +157,14 @@ __device__ void mma_pv_role_ro(const Params& p, uint8_t* smem, SmemBars* bars, c
           if (!w.wait(&bars->v_full[v.idx], v.phase)) { ok = false; break; }
           ptx::tc_fence_after();
           const uint64_t b0 = ptx::sdesc_sw128(v_base + v.idx * C::kVStage, C::kBox, 1024);
+          // P of keys 0-63 sits in columns 0-31 of the buffer, keys 64-127 in columns 64-95
           const uint32_t aP = tmem + C::kTmemS + sl * 128;
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             if (j < nsc * 4) {
               const uint32_t cb = (j >> 2) * C::kVSub + (j & 3) * 2048;
-              ptx::umma_bf16_ts(dO, aP + j * 8, desc_add(b0, cb), C::kIdescPV, (c == 0 && j == 0) ? 0u : 1u);
+              ptx::umma_bf16_ts(dO, aP + (j >> 2) * 64 + (j & 3) * 8, desc_add(b0, cb), C::kIdescPV,
+                                (c == 0 && j == 0) ? 0u : 1u);
             }
           }
           ptx::umma_commit(&bars->v_empty[v.idx]);
@@ -194,29 +199,35 @@ __device__ __forceinline__ bool ro_key_visible(const Params& p, int key, int s0,
 }
 
 template <class C>
-__device__ void softmax_role_ro(const Params& p, uint8_t* smem, SmemBars* bars, const Waiter& w, uint32_t tmem) {
+__device__ void softmax_role_ro(const Params& p, uint8_t* smem, SmemBars* bars, const Waiter& w, uint32_t tmem,
+                                int h) {
+  // Warpgroup h handles keys [64h, 64h + 64) of every chunk for all 128 rows: the row max is
+  // combined through shared memory once per chunk (one 256-thread barrier), both groups apply
+  // the same running max, group 0 rescales O, and the row sums meet at the end of the unit.
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int i = threadIdx.x - C::kSoftWarp * 32;     // 0..127 inside the warpgroup
+  const int i = threadIdx.x - (C::kSoftWarp + 4 * h) * 32;  // 0..127 inside the warpgroup
   const int quarter = warp & 3;
-  const int r = quarter * 32 + lane;                  // the row (TMEM lane) this thread owns
+  const int r = quarter * 32 + lane;                         // the row (TMEM lane) this thread owns
   const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
   float2* ml = reinterpret_cast<float2*>(smem + p.off_ml);
+  float* xmax = reinterpret_cast<float*>(smem + p.off_alpha);  // [chunk parity][half][row]
+  float* lsum1 = reinterpret_cast<float*>(smem + p.off_fac);   // [row]
   const float sl2 = p.scale_log2;
-  const int ci = r - (r / p.BQs) * p.BQs;            // token of the row inside the unit
+  const int ci = r - (r / p.BQs) * p.BQs;                   // token of the row inside the unit
   uint32_t ui = 0, ne = 0, kc = 0;
   bool dead = false;
 
   for (;; ++ui) {
     const int slot = ui % kInfoSlots;
     dead |= !w.wait_inline(&bars->info_full[slot], (ui / kInfoSlots) & 1);
-    if (ptx::named_bar_or(kWgBar0, 128, dead)) break;
+    if (ptx::named_bar_or(kWgBar0, 256, dead)) break;
     const int* inf = info_slot(p, smem, slot);
     if (inf[kInfStop]) break;
     const int nsub = min(inf[kInfNsub], p.maxsub);
     const int t0 = inf[kInfT0], kend = inf[kInfKend];
     const int nch = (nsub + 1) >> 1;
     if (nch == 0) {
-      if (i == 0) ptx::mbar_arrive(&bars->info_empty[slot]);
+      if (h == 0 && i == 0) ptx::mbar_arrive(&bars->info_empty[slot]);
       continue;
     }
     const int t = t0 + ci;
@@ -235,29 +246,32 @@ __device__ void softmax_role_ro(const Params& p, uint8_t* smem, SmemBars* bars, 
       const int sl = (int)(kc & 1u);
       dead |= !w.wait_inline(&bars->s_full[sl], (kc >> 1) & 1u);
       ptx::tc_fence_after();
-      const uint32_t sbase = tmem + lane_addr + C::kTmemS + sl * 128;
+      const uint32_t sbase = tmem + lane_addr + C::kTmemS + sl * 128 + 64 * h;
       const int s0 = inf[kInfoHdr + 2 * c];
       const bool has1 = (2 * c + 1) < nsub;
       const int s1 = has1 ? inf[kInfoHdr + 2 * c + 1] : 0;
       bool full = has1 && (max(s0, s1) + kSub - 1 <= hi_all) && (max(s0, s1) + kSub <= kend);
       if constexpr (C::kExt) full = full && (min(s0, s1) >= lo_all);
 
-      // pass 1: the row's max over the chunk
+      // pass 1: the row's max over this group's 64 keys, combined with the other group's
       float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int b = 0; b < 4; ++b) {
+      for (int b = 0; b < 2; ++b) {
         float v[32];
         ptx::tmem_ld32(sbase + 32 * b, v);
         ptx::tmem_wait_ld();
         if (!full) {
 #pragma unroll
           for (int j = 0; j < 32; ++j)
-            if (!ro_key_visible<C>(p, 32 * b + j, s0, s1, has1, hi, lo, kend)) v[j] = -INFINITY;
+            if (!ro_key_visible<C>(p, 64 * h + 32 * b + j, s0, s1, has1, hi, lo, kend)) v[j] = -INFINITY;
         }
 #pragma unroll
         for (int j = 0; j < 32; ++j) mx[j & 3] = fmaxf(mx[j & 3], v[j]);
       }
-      const float cmax_x = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * sl2;
+      float* xm = xmax + (kc & 1u) * 256;
+      xm[h * 128 + r] = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+      ptx::named_bar_sync(kWgBar0, 256);
+      const float cmax_x = fmaxf(xm[r], xm[128 + r]) * sl2;
       float m_use = m_run, alpha = 1.f;
       if (first) {
         m_use = cmax_x;
@@ -266,40 +280,40 @@ __device__ void softmax_role_ro(const Params& p, uint8_t* smem, SmemBars* bars, 
         if (m_cand > m_run + kRescaleLog2) {
           alpha = (m_run == -INFINITY) ? 0.f : ptx::ex2(m_run - m_cand);
           m_use = m_cand;
-          // this row's O, once the PV of the previous chunk (which released its buffer) is done
-          dead |= !w.wait_inline(&bars->s_empty[(kc - 1) & 1u], ((kc - 1) >> 1) & 1u);
-          ptx::tc_fence_after();
+          if (h == 0) {
+            // this row's O, once the PV of the previous chunk (which released its buffer) is done
+            dead |= !w.wait_inline(&bars->s_empty[(kc - 1) & 1u], ((kc - 1) >> 1) & 1u);
+            ptx::tc_fence_after();
 #pragma unroll
-          for (int h0 = 0; h0 < C::DV; h0 += 16) {
-            float o[16];
-            ptx::tmem_ld16(obase + h0, o);
-            ptx::tmem_wait_ld();
+            for (int h0 = 0; h0 < C::DV; h0 += 16) {
+              float o[16];
+              ptx::tmem_ld16(obase + h0, o);
+              ptx::tmem_wait_ld();
 #pragma unroll
-            for (int j = 0; j < 16; ++j) o[j] *= alpha;
-            ptx::tmem_st16(obase + h0, o);
+              for (int j = 0; j < 16; ++j) o[j] *= alpha;
+              ptx::tmem_st16(obase + h0, o);
+            }
+            ptx::tmem_wait_st();
           }
-          ptx::tmem_wait_st();
         }
       }
 
-      // pass 2: exp2, row sum, P as bf16 pairs over columns [0, 64) of the same buffer (batch b
-      // reads columns [32b, 32b+32) and writes [16b, 16b+16), all already read)
-      // (mref is finite, so a masked score of -inf gives ex2(-inf) = 0 without a select).  All
-      // four loads of the chunk come before its P stores: a tcgen05.ld issued after a
-      // tcgen05.st of the same thread waits for the store, and interleaving them per batch made
-      // this pass 2.8x slower (compressed branch at the north-star shapes, 20.8 -> 7.4 ms).
+      // pass 2: exp2, the partial row sum, and P as bf16 pairs in columns [64h, 64h + 32) of the
+      // buffer (this group's own score columns, already read).  Both loads come before the P
+      // stores: a tcgen05.ld issued after a tcgen05.st of the same thread waits for the store.
+      // (mref is finite, so a masked score of -inf gives ex2(-inf) = 0 without a select.)
       const float mref = (m_use == -INFINITY) ? 0.f : m_use;
       float ls[4] = {0.f, 0.f, 0.f, 0.f};
-      uint32_t pk[4][16];
+      uint32_t pk[2][16];
 #pragma unroll
-      for (int b = 0; b < 4; ++b) {
+      for (int b = 0; b < 2; ++b) {
         float v[32];
         ptx::tmem_ld32(sbase + 32 * b, v);
         ptx::tmem_wait_ld();
         if (!full) {
 #pragma unroll
           for (int j = 0; j < 32; ++j)
-            if (!ro_key_visible<C>(p, 32 * b + j, s0, s1, has1, hi, lo, kend)) v[j] = -INFINITY;
+            if (!ro_key_visible<C>(p, 64 * h + 32 * b + j, s0, s1, has1, hi, lo, kend)) v[j] = -INFINITY;
         }
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = ptx::ex2(fmaf(v[j], sl2, -mref));
@@ -307,12 +321,12 @@ __device__ void softmax_role_ro(const Params& p, uint8_t* smem, SmemBars* bars, 
         for (int j = 0; j < 32; ++j) ls[j & 3] += v[j];
 #pragma unroll
         for (int jj = 0; jj < 16; ++jj) {
-          const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * jj], v[2 * jj + 1]);
-          pk[b][jj] = *reinterpret_cast<const uint32_t*>(&h);
+          const __nv_bfloat162 hh = __floats2bfloat162_rn(v[2 * jj], v[2 * jj + 1]);
+          pk[b][jj] = *reinterpret_cast<const uint32_t*>(&hh);
         }
       }
 #pragma unroll
-      for (int b = 0; b < 4; ++b) ptx::tmem_st16u(sbase + 16 * b, pk[b]);
+      for (int b = 0; b < 2; ++b) ptx::tmem_st16u(sbase + 16 * b, pk[b]);
       ptx::tmem_wait_st();
       l_run = l_run * alpha + ((ls[0] + ls[1]) + (ls[2] + ls[3]));
       m_run = m_use;
@@ -322,13 +336,18 @@ __device__ void softmax_role_ro(const Params& p, uint8_t* smem, SmemBars* bars, 
       if (lane == 0) ptx::mbar_arrive(&bars->p_full[sl]);
     }
 
-    // Publish the row's running max and sum for the epilogue; the ml slot of unit ne was last
-    // read by the epilogue for unit ne - 2.
-    if (ne >= 2) dead |= !w.wait_inline(&bars->o_empty[ne & 1], ((ne >> 1) - 1) & 1);
-    ml[(ne & 1) * 128 + r] = make_float2(m_run, l_run);
-    __syncwarp();
-    if (lane == 0) ptx::mbar_arrive(&bars->wg_done[ne & 1]);
-    if (i == 0) ptx::mbar_arrive(&bars->info_empty[slot]);
+    // Row sums meet in group 0, which publishes (m, l) for the epilogue; the ml slot of unit ne
+    // was last read by the epilogue for unit ne - 2.
+    if (h == 1) lsum1[r] = l_run;
+    ptx::named_bar_sync(kWgBar0, 256);
+    if (h == 0) {
+      const float l_tot = l_run + lsum1[r];
+      if (ne >= 2) dead |= !w.wait_inline(&bars->o_empty[ne & 1], ((ne >> 1) - 1) & 1);
+      ml[(ne & 1) * 128 + r] = make_float2(m_run, l_tot);
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&bars->wg_done[ne & 1]);
+      if (i == 0) ptx::mbar_arrive(&bars->info_empty[slot]);
+    }
     ++ne;
   }
 }
@@ -453,7 +472,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     for (int s = 0; s < 2; ++s) {
       ptx::mbar_init(&bars->s_full[s], 1);   // score MMA commit
       ptx::mbar_init(&bars->s_empty[s], 1);  // PV MMA commit: P read, buffer free
-      ptx::mbar_init(&bars->p_full[s], 4);   // softmax warps
+      ptx::mbar_init(&bars->p_full[s], 8);   // softmax warps
       ptx::mbar_init(&bars->o_full[s], 1);
       ptx::mbar_init(&bars->wg_done[s], 4);
       ptx::mbar_init(&bars->o_empty[s], 4);
@@ -498,7 +517,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
   } else if (warp < C::kSoftWarp) {
     epilogue_role_ro<C>(&tmO, p, smem, bars, w, tmem);
   } else if (warp < C::kVLoadWarp) {
-    softmax_role_ro<C>(p, smem, bars, w, tmem);
+    softmax_role_ro<C>(p, smem, bars, w, tmem, (warp - C::kSoftWarp) >> 2);
   } else if (warp == C::kVLoadWarp) {
     vloader_role<C>(&tmV, p, smem, bars, w, lane);
   } else if (warp == C::kPvWarp) {
