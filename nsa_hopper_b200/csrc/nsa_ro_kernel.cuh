@@ -1,4 +1,5 @@
-// Row-owner forward for 128-row query tiles (G heads x 128/G tokens sharing one selection row).
+// Row-owner forward for 128-row query tiles (G heads x 128/G tokens sharing one selection row;
+// a 64-row tile, the reference's BQ * G = 64 mode, leaves the other 64 rows as zero padding).
 //
 // Same operation, selection semantics, unit order and loaders as nsa_sel_fwd_kernel (the
 // reference op's per-query-block mode, nsa_v2.cu:42-50, and the NSA window / compressed
@@ -389,7 +390,7 @@ __device__ void epilogue_role_ro(const CUtensorMap* tmO, const Params& p, uint8_
     }
     const float2 v_ml = nch > 0 ? ml[(ne & 1) * 128 + r] : make_float2(-INFINITY, 0.f);
     const float scale = v_ml.y > 0.f ? wgt / v_ml.y : 0.f;
-    if (ci < ntok && p.lse != nullptr) {
+    if (r < p.G * p.BQs && ci < ntok && p.lse != nullptr) {
       const float lse = v_ml.y > 0.f ? (v_ml.x + log2f(v_ml.y)) * 0.69314718055994530942f : -INFINITY;
       p.lse[((size_t)b * p.Hq + (size_t)kvh * p.G + cg) * p.T + t0 + ci] = lse;
     }
@@ -494,6 +495,12 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     bars->abort_flag = 0;
     ptx::fence_mbar_init();
   }
+  // Rows of the Q tile beyond G*BQs (a 64-row tile) are never written by TMA and must read as
+  // zero, so their score rows stay finite.
+  if (p.G * p.BQs < 128)
+    for (int idx = threadIdx.x; idx < C::kQS * C::kQBytes / 16; idx += C::kThreads)
+      reinterpret_cast<uint4*>(smem + p.off_q)[idx] = make_uint4(0u, 0u, 0u, 0u);
+  ptx::fence_proxy_async_smem();
   if (warp == kLoaderWarp && lane == 0) {
     ptx::prefetch_tmap(&tmQ);
     ptx::prefetch_tmap(&tmK);

@@ -268,11 +268,16 @@ int make_plan(const nsa_sel_desc* d, int sm_count, Plan* pl) {
   const int of32 = d->o_dtype == NSA_DTYPE_F32 ? 1 : 0;
   const char* env_ro = getenv("NSA_SEL_NO_RO");  // 1: never use the row-owner kernel (comparisons)
   int bqs = 1, ncol = 16, vi = -1;
-  if (!(env_ro != nullptr && atoi(env_ro) == 1) && d->cyc == nullptr && 128 % G == 0 && d->q_block % (128 / G) == 0) {
-    vi = find_variant(d->d_qk, d->d_v, 128, of32, ext);
-    if (vi >= 0) {
-      bqs = 128 / G;
-      ncol = 128;
+  if (!(env_ro != nullptr && atoi(env_ro) == 1) && d->cyc == nullptr) {
+    // 128 query rows per tile, or 64 (the reference's BQ * G = 64 mode) with the tile's other
+    // rows left as zero padding
+    for (int rows = 128; rows >= 64 && vi < 0; rows -= 64) {
+      if (rows % G != 0 || d->q_block % (rows / G) != 0) continue;
+      vi = find_variant(d->d_qk, d->d_v, 128, of32, ext);
+      if (vi >= 0) {
+        bqs = rows / G;
+        ncol = 128;
+      }
     }
   }
   if (vi < 0 && G > kMaxCols) return fail(NSA_ERR_UNSUPPORTED, "group size G=%d exceeds %d", G, kMaxCols);

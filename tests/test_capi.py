@@ -70,11 +70,14 @@ def test_plan_query_block_mode_splits_wide_groups(monkeypatch):
     assert p["n_cols"] == 64 and p["q_per_unit"] == 4 and p["parts"] == 4 and p["n_units"] == 48 * 4
 
 
-def test_plan_row_owner_needs_whole_128_row_tiles():
-    # BQ * G = 64 (the reference's own mode) stays on the swap-AB kernel; G = 128 takes one token
-    assert capi.plan(_desc(heads_q=32, heads_kv=2, q_block=4, n_qblocks=16384, o_dtype=capi.DTYPE_F32))["n_cols"] == 64
+def test_plan_row_owner_tiles():
+    # BQ * G = 64 (the reference's own mode): a 64-row tile of the row-owner kernel (zero padded)
+    p = capi.plan(_desc(heads_q=32, heads_kv=2, q_block=4, n_qblocks=16384, o_dtype=capi.DTYPE_F32))
+    assert p["n_cols"] == 128 and p["q_per_unit"] == 4
+    # G = 128 takes one token per tile; BQ * G = 32 stays on the swap-AB kernel
     p = capi.plan(_desc(heads_q=128, heads_kv=1))
     assert p["n_cols"] == 128 and p["q_per_unit"] == 1
+    assert capi.plan(_desc(heads_q=32, heads_kv=4, q_block=4, n_qblocks=16384))["n_cols"] == 32
     # the reference op's cycle counters are only filled by the swap-AB kernel
     assert capi.plan(_desc(q_block=8, n_qblocks=8192, cyc=256))["n_cols"] == 64
 

@@ -1,6 +1,6 @@
-"""The row-owner kernel (nsa_ro_kernel.cuh: 128 query rows per unit on the MMA's M, P in tensor
-memory) against the oracle, on the shapes that route to it: G * BQ covering whole 128-row tiles
-(128 % G == 0 and BQ % (128 / G) == 0)."""
+"""The row-owner kernel (nsa_ro_kernel.cuh: query rows on the MMA's M, P in tensor memory)
+against the oracle, on the shapes that route to it: tiles of 128 query rows, or 64 with the rest
+zero padding (G divides the tile's rows and BQ is a multiple of rows / G)."""
 import numpy as np
 import pytest
 import torch
@@ -14,7 +14,7 @@ pytestmark = pytest.mark.gpu
 
 def _routes_to_row_owner(Hq, Hkv, BQ):
     G = Hq // Hkv
-    return 128 % G == 0 and BQ % (128 // G) == 0
+    return any(rows % G == 0 and BQ % (rows // G) == 0 for rows in (128, 64))
 
 
 @pytest.mark.parametrize("B,Hq,Hkv,S,D,KSEL,BQ,lp,f32", [
@@ -25,6 +25,9 @@ def _routes_to_row_owner(Hq, Hkv, BQ):
     (1, 64, 2, 777, 64, 5, 4, 256, True),       # G = 32, l' = 256
     (1, 1, 1, 700, 128, 4, 128, 64, False),     # G = 1: 128 tokens share a row
     (1, 16, 1, 768, 64, 6, 16, 64, True),       # BQ = 16: two tiles per query block
+    (1, 32, 2, 1000, 128, 16, 4, 64, True),     # 64-row tiles (BQ * G = 64, the reference's mode)
+    (1, 8, 2, 2048, 128, 16, 16, 64, False),    # 64-row tiles, G = 4
+    (1, 4, 4, 512, 64, 4, 64, 128, True),       # 64-row tiles, G = 1
 ])
 def test_row_owner_matches_oracle(B, Hq, Hkv, S, D, KSEL, BQ, lp, f32):
     assert _routes_to_row_owner(Hq, Hkv, BQ)
