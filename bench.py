@@ -20,6 +20,7 @@ from __future__ import annotations
 import argparse
 import datetime
 import json
+import math
 import os
 import re
 import statistics
@@ -341,6 +342,69 @@ def run_ours(args, rank, world, local_rank):
 FP32_FMA_PEAK_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12  # nominal: 148 SMs x 128 FP32 lanes x FMA at max clock
 
 
+# The reference's own published sweep rows (per-query-block selection, fp32 O, its
+# results/sweep2_unstaged.csv on an H200 at 1980 MHz): (G, BQ, D, LP, S, KSEL, v2 median ms).
+REF_SWEEP_ROWS = [
+    (16, 4, 128, 64, 32768, 16, 5.009), (16, 4, 128, 64, 32768, 32, 7.1844),
+    (4, 16, 128, 64, 32768, 16, 1.302), (16, 4, 128, 128, 16384, 32, 10.5025),
+    (16, 4, 128, 256, 32768, 32, 64.1757),
+]
+
+
+def run_refsweep(args):
+    """--stage refsweep: the reference harness's protocol (sweep2.py: Hkv = 2, Hq = G * Hkv, one
+    random permutation prefix of the visible blocks per query block shared by all heads, fp32 O
+    through the reference op's signature, median of timed launches) on the rows for which the
+    reference publishes a time, with the same FLOP count (whole selected blocks)."""
+    import torch
+
+    from nsa_hopper_b200 import ops
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    gen = torch.Generator(device=dev).manual_seed(args.seed)
+    rows = []
+    with ClockSampler(0) as clk:
+        for G, BQ, D, LP, S, KSEL, ref_ms in REF_SWEEP_ROWS:
+            Hkv, B = 2, 1
+            Hq, NQB, nblk = G * Hkv, (S + BQ - 1) // BQ, S // LP
+            q = torch.randn(B, Hq, S, D, device=dev, generator=gen).to(torch.bfloat16)
+            k = torch.randn(B, Hkv, S, D, device=dev, generator=gen).to(torch.bfloat16)
+            v = torch.randn(B, Hkv, S, D, device=dev, generator=gen).to(torch.bfloat16)
+            qb = torch.arange(NQB, device=dev)
+            avail = torch.clamp((qb * BQ) // LP + 1, min=1)
+            key = torch.rand(NQB, nblk, device=dev, generator=gen)
+            key = torch.where(torch.arange(nblk, device=dev).view(1, -1) < avail.view(-1, 1), key,
+                              torch.full_like(key, 2.0))
+            perm = key.argsort(dim=1)[:, :KSEL].to(torch.int32)
+            keep = torch.arange(KSEL, device=dev).view(1, -1) < torch.clamp(avail, max=KSEL).view(-1, 1)
+            sel = torch.where(keep, perm, torch.full_like(perm, -1)).view(1, 1, NQB, KSEL).expand(
+                B, Hkv, NQB, KSEL).contiguous()
+            for _ in range(args.warmup):
+                ops.forward(q, k, v, sel, LP, BQ)
+            ts = []
+            for _ in range(max(args.steps, 5)):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                ops.forward(q, k, v, sel, LP, BQ)
+                e1.record()
+                torch.cuda.synchronize()
+                ts.append(e0.elapsed_time(e1))
+            ms = statistics.median(ts)
+            nsel = float((sel[0, 0] >= 0).float().sum().item()) / NQB
+            flops = 2 * 2 * B * Hq * NQB * BQ * nsel * LP * D
+            rows.append({"G": G, "BQ": BQ, "D": D, "LP": LP, "S": S, "KSEL": KSEL, "ms": round(ms, 4),
+                         "tflops": round(flops / (ms * 1e-3) / 1e12, 1), "ref_h200_ms": ref_ms,
+                         "speedup_vs_ref": round(ref_ms / ms, 2)})
+            del q, k, v, sel
+    geo = math.exp(sum(math.log(r["speedup_vs_ref"]) for r in rows) / len(rows))
+    return {"metric": "reference sweep rows: ms per launch vs the reference's published H200 ms",
+            "value": round(geo, 3), "unit": "geomean speed-up", "n_gpus": 1, "steps": max(args.steps, 5),
+            "warmup": args.warmup, "higher_is_better": True, "dtype": "bf16 (fp32 O)",
+            "data": "synthetic: N(0,1) bf16 Q/K/V, sweep2.py selection rule", "config": {"workload": "refsweep"},
+            "rows": rows, "clocks": clk.summary()}
+
+
 def run_select(args):
     """--stage select: the block-selection kernel (nsa_sel_select) on the workload's shapes.
     Algorithmic work per (b, kvh, token t): the group sum of G query rows (G*d adds) and one
@@ -533,9 +597,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gather", action="store_true", help="skip the separately timed all-gather (N > 1)")
-    ap.add_argument("--stage", choices=["selected", "select", "nsa"], default="selected",
+    ap.add_argument("--stage", choices=["selected", "select", "nsa", "refsweep"], default="selected",
                     help="selected: the selected-branch forward (the headline); select: the block-selection kernel; "
-                         "nsa: the full NSA forward")
+                         "nsa: the full NSA forward; refsweep: the reference's published sweep rows")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -543,9 +607,10 @@ def main():
     rank = _env_int("RANK", 0)
     local_rank = _env_int("LOCAL_RANK", 0)
 
-    if args.stage in ("select", "nsa"):
+    if args.stage in ("select", "nsa", "refsweep"):
         if rank == 0:
-            print(json.dumps(run_select(args) if args.stage == "select" else run_nsa(args)), flush=True)
+            fn = {"select": run_select, "nsa": run_nsa, "refsweep": run_refsweep}[args.stage]
+            print(json.dumps(fn(args)), flush=True)
         return
 
     if args.impl == "reference":
