@@ -115,3 +115,35 @@ def test_row_owner_compressed_branch_accumulates(T, D):
     o, _ = ops.forward_ext(q, Kc, Vc, sel, 64, bq, key_map=1, out=base.clone(), weight=w, accumulate=True)
     torch.cuda.synchronize()
     assert (o - (base + 0.25 * ref)).abs().max().item() <= 1e-2
+
+
+def test_row_owner_varlen():
+    """G = 64 with per-token rows of a packed varlen batch: 64-row tiles of one token each, block
+    ids relative to each sequence start, lengths not multiples of 64."""
+    lens = [300, 77, 1000, 64, 129]
+    Hq, Hkv, D, n = 64, 1, 64, 8
+    T = sum(lens)
+    assert _routes_to_row_owner(Hq, Hkv, 1)
+    q, k, v = make_qkv(1, Hq, Hkv, T, D, D, seed=21)
+    sel = indices.varlen_rule0(lens, Hkv, n, 64, seed=21)
+    cu = indices.cu_seqlens_of(lens)
+    o, lse = run_capi(q, k, v, torch.from_numpy(sel), cu_seqlens=torch.from_numpy(cu))
+    torch.cuda.synchronize()
+    o_ref, lse_ref = oracle.forward(q, k, v, sel, 64, 1, cu_seqlens=cu)
+    compare(o, lse, o_ref, lse_ref)
+
+
+def test_row_owner_shards_compose():
+    """Disjoint (b*Hkv+kvh, query-block) shards reproduce the full row-owner launch bit for bit."""
+    B, Hq, Hkv, T, D, n, BQ = 2, 32, 2, 1024, 128, 16, 8
+    q, k, v = make_qkv(B, Hq, Hkv, T, D, D, seed=22)
+    sel = torch.from_numpy(indices.perm_qblock(B, Hkv, T, n, BQ, 64, seed=22, heads_share=False))
+    o_full, l_full = run_capi(q, k, v, sel, BQ=BQ)
+    o_sh = torch.full_like(o_full, float("nan"))
+    l_sh = torch.full_like(l_full, float("nan"))
+    for bkv in [(0, 1), (1, 4)]:
+        for qb in [(0, 50), (50, 128)]:
+            run_capi(q, k, v, sel, BQ=BQ, shard=(bkv[0], bkv[1], qb[0], qb[1]), o=o_sh, lse=l_sh)
+    torch.cuda.synchronize()
+    assert torch.equal(o_full.view(torch.int16), o_sh.view(torch.int16))
+    assert torch.equal(l_full, l_sh)
