@@ -44,6 +44,7 @@ def _desc(q, k, v, sel, cu, o, lse, BQ, o_f32, **kw):
     (2, 16, 2, 3000, 64, 8, 4, True, 3, False),
     (1, 32, 8, 5000, 128, 16, 1, False, 5, True),
     (1, 8, 1, 777, 64, 4, 2, True, 0, False),
+    (1, 64, 4, 2048, 128, 16, 8, False, 3, False),  # 128-row tiles: the row-owner kernel
 ])
 def test_host_path_equals_device_launch(B, Hq, Hkv, T, D, n, BQ, o_f32, slices, varlen):
     q, k, v, sel, cu = _case(B, Hq, Hkv, T, D, n, BQ, o_f32, T + n, varlen)
