@@ -13,7 +13,11 @@
  * library (16 MB) that only nsa_sel_select_noalloc uses.  All launches go to the stream
  * passed in; a call returns as soon as the work is queued (like the reference op, which is
  * asynchronous on the legacy stream).  The library is reentrant: concurrent calls from
- * several host threads are safe; the error text is kept per host thread.
+ * several host threads are safe, and the error text is kept per host thread.  Two exceptions
+ * share device state between calls: nsa_sel_select_noalloc (one static scratch per device:
+ * calls on one device must be serialised, e.g. on one stream), and replays of one captured CUDA
+ * graph (each captured forward launch owns one work-counter slot: replays of the same graph
+ * must not overlap each other).
  *
  * Layouts (all contiguous, row-major, as in the reference):
  *   Q   bf16 [B, Hq,  T, d_qk]        K bf16 [B, Hkv, T, d_qk]      V bf16 [B, Hkv, T, d_v]
@@ -58,6 +62,10 @@ typedef struct CUstream_st* nsa_stream_t;
 /* Test hook: the MMA warp starts with a wait that nothing completes, so the launch ends through
    the bounded-wait error path (NSA_DEVERR_TIMEOUT after timeout_ms) without any fault. */
 #define NSA_DEBUG_STALL 1
+/* Comparison switches (same results, different schedule): hand out work units in fixed strides
+   instead of from the dynamic counter; never use the row-owner kernel for 64/128-row tiles. */
+#define NSA_DEBUG_STATIC_UNITS 2
+#define NSA_DEBUG_NO_ROW_OWNER 4
 
 #define NSA_DTYPE_BF16 0
 #define NSA_DTYPE_F32 1

@@ -25,6 +25,8 @@ NSA_ERR_CUDA = -3
 NSA_ERR_DRIVER = -4
 NSA_DEVERR_TIMEOUT = 1
 NSA_DEBUG_STALL = 1
+NSA_DEBUG_STATIC_UNITS = 2
+NSA_DEBUG_NO_ROW_OWNER = 4
 DTYPE_BF16 = 0
 DTYPE_F32 = 1
 KEYMAP_CAUSAL = 0

@@ -92,15 +92,19 @@ __device__ void mma_s_role_ro(const Params& p, uint8_t* smem, SmemBars* bars, co
       const int* inf = info_slot(p, smem, slot);
       if (inf[kInfStop]) break;
       const int nsub = min(inf[kInfNsub], p.maxsub);
+      const int ref = inf[kInfRef];
       const int nch = (nsub + 1) >> 1;
       if (nch > 0) {
         const int qs = ne % C::kQS;
+        long long t_wait = 0;
         if (!w.wait(&bars->q_full[qs], (ne / C::kQS) & 1)) break;
         const uint64_t aq0 = ptx::sdesc_sw128(q_base + qs * C::kQBytes, 16, 1024);
         for (int c = 0; c < nch; ++c) {
           const int sl = (int)(kc & 1u);
           if (kc >= 2 && !w.wait(&bars->s_empty[sl], ((kc >> 1) - 1u) & 1u)) { ok = false; break; }
+          const long long t0 = clock64();
           if (!w.wait(&bars->k_full[k.idx], k.phase)) { ok = false; break; }
+          t_wait += clock64() - t0;
           ptx::tc_fence_after();
           const uint64_t bk0 = ptx::sdesc_sw128(k_base + k.idx * C::kKStage, 16, 1024);
           const uint32_t dS = tmem + C::kTmemS + sl * 128;
@@ -117,6 +121,9 @@ __device__ void mma_s_role_ro(const Params& p, uint8_t* smem, SmemBars* bars, co
         }
         if (!ok) break;
         ptx::umma_commit(&bars->q_empty[qs]);
+        // the reference op's cycle counters (nsa_v2.cu:69-71): K-tile wait cycles of the unit
+        if (p.cyc != nullptr) atomicAdd(reinterpret_cast<unsigned long long*>(p.cyc + 2 * (size_t)ref),
+                                        (unsigned long long)t_wait);
         ++ne;
       }
       ptx::mbar_arrive(&bars->info_empty[slot]);
@@ -146,8 +153,11 @@ __device__ void mma_pv_role_ro(const Params& p, uint8_t* smem, SmemBars* bars, c
       const int* inf = info_slot(p, smem, slot);
       if (inf[kInfStop]) break;
       const int nsub = min(inf[kInfNsub], p.maxsub);
+      const int ref = inf[kInfRef];
       const int nch = (nsub + 1) >> 1;
       if (nch > 0) {
+        const long long t_unit0 = clock64();
+        long long t_wait = 0;
         // this O buffer (and the unit's ml slot) was last read by the epilogue for unit ne - 2
         if (ne >= 2 && !w.wait(&bars->o_empty[ne & 1], ((ne >> 1) - 1) & 1)) break;
         const uint32_t dO = tmem + C::kTmemO + (ne & 1) * C::DV;
@@ -155,7 +165,9 @@ __device__ void mma_pv_role_ro(const Params& p, uint8_t* smem, SmemBars* bars, c
           const int sl = (int)(kc & 1u);
           const int nsc = min(2, nsub - 2 * c);
           if (!w.wait(&bars->p_full[sl], (kc >> 1) & 1u)) { ok = false; break; }
+          const long long t0 = clock64();
           if (!w.wait(&bars->v_full[v.idx], v.phase)) { ok = false; break; }
+          t_wait += clock64() - t0;
           ptx::tc_fence_after();
           const uint64_t b0 = ptx::sdesc_sw128(v_base + v.idx * C::kVStage, C::kBox, 1024);
           // P of keys 0-63 sits in columns 0-31 of the buffer, keys 64-127 in columns 64-95
@@ -175,6 +187,13 @@ __device__ void mma_pv_role_ro(const Params& p, uint8_t* smem, SmemBars* bars, c
         }
         if (!ok) break;
         ptx::umma_commit(&bars->o_full[ne & 1]);
+        // cycle counters: V-tile wait cycles, and the unit's other cycles on this warp
+        if (p.cyc != nullptr) {
+          const long long tot = clock64() - t_unit0;
+          atomicAdd(reinterpret_cast<unsigned long long*>(p.cyc + 2 * (size_t)ref), (unsigned long long)t_wait);
+          atomicAdd(reinterpret_cast<unsigned long long*>(p.cyc + 2 * (size_t)ref + 1),
+                    (unsigned long long)(tot > t_wait ? tot - t_wait : 0));
+        }
         ++ne;
       }
       ptx::mbar_arrive(&bars->info_empty[slot]);
@@ -539,6 +558,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, C::kTmemCols);
   }
+  if (threadIdx.x == 0) release_work_counter(p);
 }
 
 }  // namespace nsa

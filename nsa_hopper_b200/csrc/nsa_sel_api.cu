@@ -68,25 +68,45 @@ DeviceCache g_dev;
 
 }  // namespace
 
-// Unit counters of the dynamic work distribution (Params::work_counter): one 4-byte slot per
-// launch, taken round-robin and zeroed on the launch's stream just before it, so launches in
-// flight on different streams use different slots.  Static device memory: nothing is allocated.
-constexpr int kWorkCounterSlots = 4096;
-__device__ unsigned int g_work_counters[kWorkCounterSlots];
+// Unit counters of the dynamic work distribution (Params::work_counter): slots of two words
+// {next unit, finished CTAs} in static device memory (nothing is allocated).  A slot is zero at
+// module load and the last CTA of every launch zeroes it again, so no reset is queued before a
+// launch.  Launches that are not being captured take the eager slots round-robin, so launches in
+// flight on different streams use different slots.  A launch captured into a CUDA graph keeps its
+// slot for every replay, so each capture takes a slot of its own that is never handed out again;
+// when those run out, further captured launches use the fixed-stride schedule (no counter).
+constexpr int kEagerCounterSlots = 2048;
+constexpr int kCaptureCounterSlots = 2048;
+__device__ unsigned int g_work_counters[2 * (kEagerCounterSlots + kCaptureCounterSlots)];
 
 namespace {
 unsigned int* g_work_counter_base[kMaxDevices] = {};
 unsigned int g_work_counter_next[kMaxDevices] = {};
+unsigned int g_capture_counter_next[kMaxDevices] = {};
 
-int next_work_counter(int dev, unsigned int** out) {
+// *out = the slot for a launch on `stream`, or nullptr for the fixed-stride schedule.
+int next_work_counter(int dev, cudaStream_t stream, unsigned int** out) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  cudaError_t e = cudaStreamIsCapturing(stream, &cs);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamIsCapturing");
   std::lock_guard<std::mutex> lk(g_dev.mu);
   if (g_work_counter_base[dev] == nullptr) {
     void* ptr = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&ptr, g_work_counters);
+    e = cudaGetSymbolAddress(&ptr, g_work_counters);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(work counters)");
     g_work_counter_base[dev] = static_cast<unsigned int*>(ptr);
   }
-  *out = g_work_counter_base[dev] + (g_work_counter_next[dev]++ % (unsigned)kWorkCounterSlots);
+  unsigned int slot;
+  if (cs == cudaStreamCaptureStatusActive) {
+    if (g_capture_counter_next[dev] >= (unsigned)kCaptureCounterSlots) {
+      *out = nullptr;
+      return NSA_OK;
+    }
+    slot = kEagerCounterSlots + g_capture_counter_next[dev]++;
+  } else {
+    slot = g_work_counter_next[dev]++ % (unsigned)kEagerCounterSlots;
+  }
+  *out = g_work_counter_base[dev] + 2 * slot;
   return NSA_OK;
 }
 
@@ -266,9 +286,8 @@ int make_plan(const nsa_sel_desc* d, int sm_count, Plan* pl) {
   // of BQ with G * tokens <= 64 goes to the swap-AB kernel (keys on M).
   const int ext = (d->window > 0 || d->key_map != NSA_KEYMAP_CAUSAL) ? 1 : 0;
   const int of32 = d->o_dtype == NSA_DTYPE_F32 ? 1 : 0;
-  const char* env_ro = getenv("NSA_SEL_NO_RO");  // 1: never use the row-owner kernel (comparisons)
   int bqs = 1, ncol = 16, vi = -1;
-  if (!(env_ro != nullptr && atoi(env_ro) == 1) && d->cyc == nullptr) {
+  if (!(d->debug_flags & NSA_DEBUG_NO_ROW_OWNER)) {
     // 128 query rows per tile, or 64 (the reference's BQ * G = 64 mode) with the tile's other
     // rows left as zero padding
     for (int rows = 128; rows >= 64 && vi < 0; rows -= 64) {
@@ -333,15 +352,6 @@ int make_plan(const nsa_sel_desc* d, int sm_count, Plan* pl) {
   if (ks < nsa::kMaxStages && fits(ks + 1, vs)) ++ks;
   // With one PV warp per softmax group the V stages are split between them: keep a multiple.
   const int vmult = V.vgroups;
-  const char* env_ks = getenv("NSA_SEL_KSTAGES");
-  const char* env_vs = getenv("NSA_SEL_VSTAGES");
-  if (env_ks != nullptr || env_vs != nullptr) {
-    const int eks = env_ks ? atoi(env_ks) : ks, evs = env_vs ? atoi(env_vs) : vs;
-    if (eks >= 1 && evs >= 1 && eks <= nsa::kMaxStages && evs <= nsa::kMaxStages && fits(eks, evs)) {
-      ks = eks;
-      vs = evs;
-    }
-  }
   if (vmult > 1) vs -= vs % vmult;
   if (vs < vmult) return fail(NSA_ERR_UNSUPPORTED, "tile does not fit in shared memory");
   pl->KS = ks;
@@ -488,14 +498,9 @@ int launch(const nsa_sel_desc* d, nsa_stream_t stream) {
     }
   }
   p.work_counter = nullptr;
-  const char* env_static = getenv("NSA_SEL_STATIC_UNITS");  // 1: fixed strides (for comparisons)
-  if (pl.n_units > pl.grid && !(env_static != nullptr && atoi(env_static) == 1)) {
-    unsigned int* wc = nullptr;
-    rc = next_work_counter(dev, &wc);
+  if (pl.n_units > pl.grid && !(d->debug_flags & NSA_DEBUG_STATIC_UNITS)) {
+    rc = next_work_counter(dev, reinterpret_cast<cudaStream_t>(stream), &p.work_counter);
     if (rc != NSA_OK) return rc;
-    cudaError_t me = cudaMemsetAsync(wc, 0, sizeof(unsigned int), reinterpret_cast<cudaStream_t>(stream));
-    if (me != cudaSuccess) return cuda_fail(me, "cudaMemsetAsync(work counter)");
-    p.work_counter = wc;
   }
   void* args[] = {&tmQ, &tmK, &tmV, &tmO, &p};
   cudaError_t e = cudaLaunchKernel(reinterpret_cast<const void*>(V.kernel), dim3(pl.grid), dim3(V.threads), args,

@@ -27,6 +27,8 @@ def plan(B: int, Hkv: int, T: int, world: int, top_n: int = 16, block: int = 64)
     rows = B * Hkv
     if world <= 0:
         raise ValueError("world must be positive")
+    if world > rows * T:
+        raise ValueError(f"world={world} exceeds the {rows * T} (batch*KV-head, token) rows to share")
     if world <= rows and rows % world == 0:
         per = rows // world
         return [[(r * per, (r + 1) * per, 0, T)] for r in range(world)]
@@ -56,13 +58,18 @@ def plan(B: int, Hkv: int, T: int, world: int, top_n: int = 16, block: int = 64)
 
 
 def _balanced_cuts(cost: np.ndarray, k: int) -> List[int]:
+    """k + 1 strictly increasing cuts 0 = c_0 < ... < c_k = len(cost) that split `cost` into k
+    non-empty ranges of nearly equal total cost."""
+    n = len(cost)
+    if k <= 0 or k > n:
+        raise ValueError(f"cannot cut {n} rows into {k} non-empty ranges")
     c = np.concatenate([[0.0], np.cumsum(cost)])
     targets = c[-1] * np.arange(1, k) / k
     inner = np.searchsorted(c, targets, side="left").tolist()
-    cuts = [0] + [int(x) for x in inner] + [len(cost)]
-    for i in range(1, len(cuts)):  # keep cuts strictly increasing
-        cuts[i] = max(cuts[i], cuts[i - 1] + (1 if i < len(cuts) - 1 else 0))
-    cuts[-1] = len(cost)
+    cuts = [0] + [int(x) for x in inner] + [n]
+    for i in range(1, k):  # strictly increasing, and room left for the ranges after cut i
+        cuts[i] = min(max(cuts[i], cuts[i - 1] + 1), n - (k - i))
+    cuts[k] = n
     return cuts
 
 

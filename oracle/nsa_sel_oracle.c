@@ -51,6 +51,9 @@ typedef struct {
   const int32_t* cu;
   int n_seqs, B, Hq, Hkv, T, dqk, dv, NQB, KSEL, LP, BQ, strict;
   double scale;
+  /* q, o and lse hold tokens [tq0, tq0 + Tq) of every (b, head): the full sequence (tq0 = 0,
+     Tq = T) or only the computed row window (the *_window entry points). */
+  int tq0, Tq;
 } oracle_args;
 
 /* Locate the sequence [c0, c1) holding token t (whole range when not varlen). */
@@ -128,7 +131,7 @@ static int visible_keys(const oracle_args* a, int b, int kvh, int t, unsigned ch
           for (int d = 0; d < a->dqk; ++d) kf[(size_t)j * a->dqk + d] = bf16_to_f32(kbase[(size_t)keys[j] * a->dqk + d]); \
         for (int g = 0; g < G; ++g) {                                                                         \
           const int h = kvh * G + g;                                                                          \
-          const size_t qrow = ((size_t)(b * a->Hq + h) * a->T + t);                                           \
+          const size_t qrow = ((size_t)(b * a->Hq + h) * a->Tq + (t - a->tq0));                               \
           for (int d = 0; d < a->dqk; ++d) qf[d] = bf16_to_f32(a->q[qrow * a->dqk + d]);                      \
           REAL mx = -INFINITY;                                                                                \
           for (int j = 0; j < n; ++j) {                                                                       \
@@ -185,16 +188,20 @@ static int check_args(const oracle_args* a, int bkv_begin, int bkv_end, int t_be
   return NSA_ORACLE_OK;
 }
 
-#define ORACLE_SETUP()                                                                                        \
+#define ORACLE_SETUP(WINDOW)                                                                                  \
   oracle_args A = {q, k, v, sel, cu_seqlens, n_seqs, B, Hq, Hkv, T, dqk, dv, NQB, KSEL, LP, BQ, strict,      \
-                   scale > 0 ? scale : 1.0 / sqrt((double)dqk)};                                              \
-  const oracle_args* a = &A;                                                                                  \
+                   scale > 0 ? scale : 1.0 / sqrt((double)dqk), 0, T};                                        \
+  oracle_args* a = &A;                                                                                        \
   if (bkv_end <= 0) bkv_end = B * Hkv;                                                                        \
   if (t_end <= 0) t_end = T;                                                                                  \
   if (nthreads <= 0) nthreads = 1;                                                                            \
   {                                                                                                           \
     int rc = check_args(a, bkv_begin, bkv_end, t_begin, t_end, o);                                            \
     if (rc) return rc;                                                                                        \
+  }                                                                                                           \
+  if (WINDOW) {                                                                                               \
+    a->tq0 = t_begin;                                                                                         \
+    a->Tq = t_end - t_begin;                                                                                  \
   }
 
 /* Rows (b*Hkv+kvh in [bkv_begin, bkv_end), t in [t_begin, t_end)) are computed; others are
@@ -203,7 +210,7 @@ int nsa_oracle_forward(const uint16_t* q, const uint16_t* k, const uint16_t* v, 
                        const int32_t* cu_seqlens, int n_seqs, int B, int Hq, int Hkv, int T, int dqk, int dv,
                        int NQB, int KSEL, int LP, int BQ, double scale, int bkv_begin, int bkv_end, int t_begin,
                        int t_end, int strict, double* o, double* lse, int nthreads) {
-  ORACLE_SETUP();
+  ORACLE_SETUP(0);
   ORACLE_BODY(double, exp, log)
 }
 
@@ -211,7 +218,27 @@ int nsa_oracle_forward_f32(const uint16_t* q, const uint16_t* k, const uint16_t*
                            const int32_t* cu_seqlens, int n_seqs, int B, int Hq, int Hkv, int T, int dqk, int dv,
                            int NQB, int KSEL, int LP, int BQ, double scale, int bkv_begin, int bkv_end,
                            int t_begin, int t_end, int strict, float* o, float* lse, int nthreads) {
-  ORACLE_SETUP();
+  ORACLE_SETUP(0);
+  ORACLE_BODY(float, expf, logf)
+}
+
+/* The same rows, with q, o and lse holding only tokens [t_begin, t_end) of every (b, head):
+   q [B, Hq, t_end - t_begin, dqk], o [B, Hq, t_end - t_begin, dv], lse [B, Hq, t_end - t_begin]
+   (k, v and sel stay whole: the gather reaches any earlier key).  For parity checks of long
+   sequences without a host copy of the whole Q and O. */
+int nsa_oracle_forward_window(const uint16_t* q, const uint16_t* k, const uint16_t* v, const int32_t* sel,
+                              const int32_t* cu_seqlens, int n_seqs, int B, int Hq, int Hkv, int T, int dqk, int dv,
+                              int NQB, int KSEL, int LP, int BQ, double scale, int bkv_begin, int bkv_end,
+                              int t_begin, int t_end, int strict, double* o, double* lse, int nthreads) {
+  ORACLE_SETUP(1);
+  ORACLE_BODY(double, exp, log)
+}
+
+int nsa_oracle_forward_window_f32(const uint16_t* q, const uint16_t* k, const uint16_t* v, const int32_t* sel,
+                                  const int32_t* cu_seqlens, int n_seqs, int B, int Hq, int Hkv, int T, int dqk,
+                                  int dv, int NQB, int KSEL, int LP, int BQ, double scale, int bkv_begin, int bkv_end,
+                                  int t_begin, int t_end, int strict, float* o, float* lse, int nthreads) {
+  ORACLE_SETUP(1);
   ORACLE_BODY(float, expf, logf)
 }
 

@@ -41,6 +41,10 @@ def _load():
     lib.nsa_oracle_forward.restype = i
     lib.nsa_oracle_forward_f32.argtypes = common
     lib.nsa_oracle_forward_f32.restype = i
+    lib.nsa_oracle_forward_window.argtypes = common
+    lib.nsa_oracle_forward_window.restype = i
+    lib.nsa_oracle_forward_window_f32.argtypes = common
+    lib.nsa_oracle_forward_window_f32.restype = i
     lib.nsa_oracle_count_keys.argtypes = [p, p, i, i, i, i, i, i, i, i, p, i]
     lib.nsa_oracle_count_keys.restype = i
     _lib = lib
@@ -109,6 +113,35 @@ def forward(q, k, v, sel, l_prime: int, BQ: int, *, cu_seqlens=None, scale: floa
             threads if threads else default_threads())
     if rc == ERR_INDEX:
         raise IndexError("selection holds a block id greater than the block count")
+    if rc != 0:
+        raise ValueError(f"oracle rejected the arguments (code {rc})")
+    return o, lse
+
+
+def forward_window(q_win, k, v, sel, l_prime: int, BQ: int, t_range: Tuple[int, int], *, cu_seqlens=None,
+                   scale: float = 0.0, f32: bool = True, bkv_range: Optional[Tuple[int, int]] = None,
+                   threads: Optional[int] = None):
+    """``forward`` on the token rows ``t_range`` = [t0, t1) only, with ``q_win`` holding just those
+    rows: q_win [B,Hq,t1-t0,dqk]; k, v and sel whole (T = k.shape[2]).  Returns (O [B,Hq,t1-t0,dv],
+    LSE [B,Hq,t1-t0]) for the rows of ``bkv_range`` (others NaN); float32 by default."""
+    lib = _load()
+    qb, kb, vb = _bits(q_win), _bits(k), _bits(v)
+    s = _i32(sel)
+    B, Hq, nt, dqk = qb.shape
+    Hkv, T, dv = kb.shape[1], kb.shape[2], vb.shape[3]
+    t0, t1 = t_range
+    if t1 - t0 != nt or not (0 <= t0 < t1 <= T):
+        raise ValueError(f"q_win holds {nt} rows, t_range {t_range} for T={T}")
+    NQB, KSEL = s.shape[2], s.shape[3]
+    dt = np.float32 if f32 else np.float64
+    o = np.full((B, Hq, nt, dv), np.nan, dtype=dt)
+    lse = np.full((B, Hq, nt), np.nan, dtype=dt)
+    cu = None if cu_seqlens is None else _i32(cu_seqlens)
+    n_seqs = 0 if cu is None else len(cu) - 1
+    b0, b1 = bkv_range if bkv_range is not None else (0, B * Hkv)
+    fn = lib.nsa_oracle_forward_window_f32 if f32 else lib.nsa_oracle_forward_window
+    rc = fn(_ptr(qb), _ptr(kb), _ptr(vb), _ptr(s), _ptr(cu), n_seqs, B, Hq, Hkv, T, dqk, dv, NQB, KSEL, l_prime, BQ,
+            float(scale), b0, b1, t0, t1, 0, _ptr(o), _ptr(lse), threads if threads else default_threads())
     if rc != 0:
         raise ValueError(f"oracle rejected the arguments (code {rc})")
     return o, lse

@@ -57,16 +57,15 @@ def test_plan_north_star():
     assert p["smem_bytes"] <= 232448 and p["k_stages"] >= 2 and p["v_stages"] >= 2
 
 
-def test_plan_query_block_mode_splits_wide_groups(monkeypatch):
+def test_plan_query_block_mode_splits_wide_groups():
     kw = dict(heads_q=16, heads_kv=1, seq_len=768, n_qblocks=48, n_sel=6, d_qk=64, d_v=64, q_block=16,
               o_dtype=capi.DTYPE_F32)
     # G = 16 with BQ = 16 is 256 query rows: two 128-row units for the row-owner kernel
     p = capi.plan(_desc(**kw))
     assert p["n_cols"] == 128 and p["q_per_unit"] == 8 and p["parts"] == 2 and p["n_units"] == 48 * 2
     assert p["tmem_cols"] == 512 and p["smem_bytes"] <= 232448
-    # without it (NSA_SEL_NO_RO=1): parts of 4 tokens (N = 64) for the swap-AB kernel
-    monkeypatch.setenv("NSA_SEL_NO_RO", "1")
-    p = capi.plan(_desc(**kw))
+    # without it (debug flag NSA_DEBUG_NO_ROW_OWNER): parts of 4 tokens (N = 64) for the swap-AB kernel
+    p = capi.plan(_desc(debug_flags=capi.NSA_DEBUG_NO_ROW_OWNER, **kw))
     assert p["n_cols"] == 64 and p["q_per_unit"] == 4 and p["parts"] == 4 and p["n_units"] == 48 * 4
 
 
@@ -78,8 +77,9 @@ def test_plan_row_owner_tiles():
     p = capi.plan(_desc(heads_q=128, heads_kv=1))
     assert p["n_cols"] == 128 and p["q_per_unit"] == 1
     assert capi.plan(_desc(heads_q=32, heads_kv=4, q_block=4, n_qblocks=16384))["n_cols"] == 32
-    # the reference op's cycle counters are only filled by the swap-AB kernel
-    assert capi.plan(_desc(q_block=8, n_qblocks=8192, cyc=256))["n_cols"] == 64
+    # the reference op's cycle counters do not change the kernel: both kernels fill them
+    assert capi.plan(_desc(q_block=8, n_qblocks=8192, cyc=256))["n_cols"] == 128
+    assert capi.plan(_desc(heads_q=128, heads_kv=1, cyc=256))["n_cols"] == 128
 
 
 def test_plan_small_group_pads_columns():

@@ -147,3 +147,26 @@ def test_row_owner_shards_compose():
     torch.cuda.synchronize()
     assert torch.equal(o_full.view(torch.int16), o_sh.view(torch.int16))
     assert torch.equal(l_full, l_sh)
+
+
+@pytest.mark.parametrize("Hq,Hkv,BQ,S,D", [(32, 2, 4, 1024, 128),   # 64-row tiles: the reference's BQ * G = 64
+                                           (128, 1, 1, 512, 64),    # G = 128: one token per 128-row tile
+                                           (16, 1, 8, 768, 64)])    # 128-row tiles
+def test_row_owner_fills_cycle_counters(Hq, Hkv, BQ, S, D):
+    """A non-empty cyc (the reference op's counters, nsa_v2.cu:69-71) no longer changes the kernel:
+    the row-owner kernel runs, fills every query block's counters and matches the oracle."""
+    B, KSEL, lp = 1, 6, 64
+    d = capi.make_desc(q=256, k=256, v=256, sel=256, o=256, cyc=256, batch=B, heads_q=Hq, heads_kv=Hkv, seq_len=S,
+                       d_qk=D, d_v=D, n_qblocks=(S + BQ - 1) // BQ, n_sel=KSEL, block_size=lp, q_block=BQ,
+                       o_dtype=capi.DTYPE_F32)
+    assert capi.plan(d)["n_cols"] == 128  # row-owner tiles
+    q, k, v = make_qkv(B, Hq, Hkv, S, D, D, seed=S + Hq)
+    sel = indices.perm_qblock(B, Hkv, S, KSEL, BQ, lp, seed=S)
+    NQB = sel.shape[2]
+    cyc = torch.zeros(NQB * B * Hkv * 2, dtype=torch.int64, device="cuda")
+    o = ops.forward(q.cuda(), k.cuda(), v.cuda(), torch.from_numpy(sel).cuda(), lp, BQ, cyc)
+    torch.cuda.synchronize()
+    r, _ = oracle.forward(q, k, v, sel, lp, BQ)
+    assert np.abs(o.cpu().numpy() - r).max() <= 1e-2
+    c = cyc.cpu().numpy()
+    assert (c[1::2] > 0).all() and (c >= 0).all()

@@ -9,6 +9,7 @@ import torch
 import oracle
 from nsa_hopper_b200 import indices
 from tests import golden_cases
+from tests.helpers import make_qkv
 
 
 @pytest.mark.parametrize("name", golden_cases.case_names())
@@ -111,3 +112,17 @@ def test_row_ranges_compose():
             oracle.forward(q, k, v, sel, 64, 1, bkv_range=bkv, t_range=tr, out=o2, lse_out=l2)
     np.testing.assert_array_equal(o, o2)
     np.testing.assert_array_equal(l, l2)
+
+
+def test_window_form_equals_full_rows():
+    """oracle.forward_window (Q/O/LSE holding only the computed token rows) gives exactly the
+    rows of the full-array form."""
+    q, k, v = make_qkv(2, 8, 2, 700, 64, 32, seed=3)
+    sel = indices.rule0(2, 2, 700, 8, 64, seed=3)
+    o, l = oracle.forward(q, k, v, sel, 64, 1, f32=True)
+    ow, lw = oracle.forward_window(q[:, :, 300:450].contiguous(), k, v, sel, 64, 1, (300, 450))
+    assert np.array_equal(ow, o[:, :, 300:450]) and np.array_equal(lw, l[:, :, 300:450])
+    ow, lw = oracle.forward_window(q[:, :, 650:].contiguous(), k, v, sel, 64, 1, (650, 700), bkv_range=(3, 4),
+                                   f32=False)
+    o64, l64 = oracle.forward(q, k, v, sel, 64, 1)
+    assert np.array_equal(ow[1, 4:], o64[1, 4:, 650:]) and np.isnan(ow[0]).all()

@@ -94,3 +94,42 @@ def test_shard_plan_covers_every_row_once(B, Hkv, T, world):
     cost = shard.token_cost(T)
     loads = [sum(cost[q0:q1].sum() * (b1 - b0) for b0, b1, q0, q1 in r) for r in plans]
     assert max(loads) <= 1.02 * (sum(loads) / world) + cost.max()
+
+
+def _cover_ok(B, Hkv, T, plans):
+    cover = np.zeros((B * Hkv, T), np.int32)
+    for rects in plans:
+        assert rects, "a rank received no rows"
+        for b0, b1, q0, q1 in rects:
+            assert 0 <= b0 < b1 <= B * Hkv and 0 <= q0 < q1 <= T, (b0, b1, q0, q1)
+            cover[b0:b1, q0:q1] += 1
+    return (cover == 1).all()
+
+
+def test_balanced_cuts_skewed_costs_stay_in_range():
+    """Skewed costs must not push cuts past the end (non-empty, increasing ranges)."""
+    cuts = shard._balanced_cuts(np.array([1.0, 1.0, 1.0, 100.0]), 4)
+    assert cuts == [0, 1, 2, 3, 4]
+    assert _cover_ok(1, 1, 3, shard.plan(1, 1, 3, 3))
+    with pytest.raises(ValueError):
+        shard.plan(1, 1, 3, 4)
+
+
+try:
+    from hypothesis import given, settings, strategies as st
+
+    @settings(max_examples=200, deadline=None)
+    @given(B=st.integers(1, 4), Hkv=st.integers(1, 8), T=st.integers(1, 300), world=st.integers(1, 40),
+           top_n=st.integers(1, 16), block=st.sampled_from([1, 7, 64]))
+    def test_shard_plan_property_every_row_once(B, Hkv, T, world, top_n, block):
+        """Property: whenever a plan exists, its rectangles are in range, non-empty, and cover every
+        (batch*KV-head, token) row exactly once."""
+        if world > B * Hkv * T:
+            with pytest.raises(ValueError):
+                shard.plan(B, Hkv, T, world, top_n=top_n, block=block)
+            return
+        plans = shard.plan(B, Hkv, T, world, top_n=top_n, block=block)
+        assert len(plans) == world
+        assert _cover_ok(B, Hkv, T, plans)
+except ImportError:  # pragma: no cover - hypothesis is optional
+    pass
