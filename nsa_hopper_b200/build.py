@@ -62,6 +62,22 @@ def build_kernel_lib(force: bool = False, extra: List[str] = ()) -> str:
     return LIB
 
 
+def build_peaks_lib(force: bool = False) -> str:
+    """libnsa_peaks.so: the on-chip ceiling microbenchmarks behind bench.py's roofline (measurement
+    code, not on the product path)."""
+    out = os.path.join(PKG, "libnsa_peaks.so")
+    srcs = [os.path.join(CSRC, "nsa_peaks.cu")] + sorted(
+        os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith(".cuh"))
+    if not force and not _stale(out, srcs):
+        return out
+    cmd = [NVCC, *ARCH_FLAGS, "-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-shared",
+           "-cudart", "shared", f"-I{INCLUDE}", f"-I{CSRC}", "-Xlinker", f"-rpath={CUDA_HOME}/lib64",
+           "-o", out + ".tmp", srcs[0]]
+    _run(cmd)
+    os.replace(out + ".tmp", out)
+    return out
+
+
 def build_torch_ext(force: bool = False) -> str:
     import torch
     from torch.utils import cpp_extension
@@ -86,6 +102,7 @@ def build_torch_ext(force: bool = False) -> str:
 
 def build_all(force: bool = False) -> None:
     build_kernel_lib(force)
+    build_peaks_lib(force)
     build_torch_ext(force)
 
 

@@ -558,7 +558,6 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, C::kTmemCols);
   }
-  if (threadIdx.x == 0) release_work_counter(p);
 }
 
 }  // namespace nsa

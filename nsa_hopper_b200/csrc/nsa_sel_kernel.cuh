@@ -116,10 +116,8 @@ struct Params {
   int debug_stall;  // 1: the MMA warp first waits on a barrier nothing arrives on (error-path test)
   int out_bufs;     // output staging tiles (2: double buffer; 1 when shared memory is tight)
   // Work distribution: after the first wave (unit = blockIdx.x), each CTA takes the next unit
-  // from work_counter[0], so SMs that run faster take more units; nullptr = fixed strides of
-  // gridDim.x.  The slot must read {0, 0} at launch; work_counter[1] counts finished CTAs and
-  // the last CTA to finish puts both words back to 0 (release_work_counter), so a slot needs
-  // no reset between launches that use it one after another.
+  // from this global counter, zeroed on the stream just before the launch, so SMs that run
+  // faster take more units; nullptr = fixed strides of gridDim.x.
   unsigned int* work_counter;
   int o_accum;             // 1: O += w * result through TMA reduce-add (fp32 O); 0: O = w * result
   const float* o_weight;   // device float w, or nullptr for 1
@@ -289,19 +287,6 @@ struct Waiter {
     return true;
   }
 };
-
-// Called by thread 0 of every CTA after the CTA's final __syncthreads (every role, the
-// scheduler's last counter claim included, is done).  The CTA that finishes last zeroes the slot
-// for the next launch that uses it: its fenced increment of the finish count comes after every
-// other CTA's (each fenced after its own claims), so no claim can follow the reset.
-__device__ __forceinline__ void release_work_counter(const Params& p) {
-  if (p.work_counter == nullptr) return;
-  __threadfence();
-  if (atomicAdd(p.work_counter + 1, 1u) == gridDim.x - 1) {
-    atomicExch(p.work_counter, 0u);
-    atomicExch(p.work_counter + 1, 0u);
-  }
-}
 
 __device__ __forceinline__ int key_hi(const Params& p, int t) {
   return p.key_map ? compressed_limit(t, p.T, p.kv_len) : t;
@@ -1159,7 +1144,6 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, C::kTmemCols);
   }
-  if (threadIdx.x == 0) release_work_counter(p);
 }
 
 }  // namespace nsa

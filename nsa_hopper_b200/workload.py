@@ -126,3 +126,25 @@ def algorithmic_work(w: Workload, sel: np.ndarray, T: Optional[int] = None,
         "visible_keys": keys,
         "gathered_blocks": nblk,
     }
+
+
+def rect_work(w: Workload, sel: np.ndarray, rects, T: Optional[int] = None,
+              cu_seqlens: Optional[np.ndarray] = None) -> Dict[str, float]:
+    """algorithmic_work restricted to the (bkv_begin, bkv_end, t_begin, t_end) rectangles of a
+    shard: the FLOPs, gathered K/V bytes and all bytes of the rows the rectangles cover."""
+    T = w.T if T is None else T
+    G = w.G
+    first, nvis = _distinct_visible(sel, T, w.block, cu_seqlens)
+    keys_row = nvis.sum(-1).astype(np.float64)   # [B*Hkv, T]
+    blk_row = first.sum(-1).astype(np.float64)
+    out = {"flops": 0.0, "kv_bytes": 0.0, "bytes": 0.0, "tokens": 0.0, "rows": 0.0}
+    for b0, b1, t0, t1 in rects:
+        keys = keys_row[b0:b1, t0:t1].sum()
+        nblk = blk_row[b0:b1, t0:t1].sum()
+        rows = (b1 - b0) * (t1 - t0)
+        kv = nblk * w.block * (w.d_qk + w.d_v) * 2.0
+        out["flops"] += G * 2.0 * (w.d_qk + w.d_v) * keys
+        out["kv_bytes"] += kv
+        out["bytes"] += kv + rows * G * (w.d_qk * 2.0 + w.d_v * 2.0 + 4.0) + rows * w.n * 4.0
+        out["rows"] += rows
+    return out

@@ -1,9 +1,10 @@
 """CUDA graph capture of the forward (nsa_sel_run through the C ABI).
 
-A captured launch keeps its dynamic work-counter slot for every replay, so captured launches
-take slots that eager launches never use.  The test wraps the eager slots twice (more than 4096
-eager launches), then replays the graph on one stream while eager launches run on another, and
-checks both results (a shared slot would make the two launches skip each other's work units)."""
+A captured launch keeps its dynamic work-counter slot (and the reset queued before it) for every
+replay, so captured launches take slots that eager launches never use.  The test wraps the eager
+slots twice (more than 4096 eager launches), then replays the graph on one stream while eager
+launches run on another, and checks both results (a shared slot would make the two launches skip
+each other's work units)."""
 import numpy as np
 import pytest
 import torch
@@ -41,7 +42,7 @@ def test_graph_replay_beside_eager_launches_on_another_stream():
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
         capi.run(d_g, torch.cuda.current_stream().cuda_stream)
-    # wrap the eager slots twice; the last launch reuses a slot two earlier launches released
+    # wrap the eager slots twice; the last launch reuses a slot that two earlier launches used
     for i in range(4200):
         if i == 4199:
             o_e.fill_(float("nan"))

@@ -10,8 +10,9 @@ exact -inf pattern (rows with no visible key).
 Coverage per configuration:
   ns    B=1 T=65536 Hq=64 Hkv=4 D=128 n=16, rule 0: every row of every KV head.
   cfg1  B=1 T=8192: every row.
-  cfg2  B=4 T=32768, 30 % reuse: Q and O are 2.15 GB (byte offsets past 2^31); rows 0 and 15
-        (the first and the highest addresses) whole, a 2048-token range of every other row.
+  cfg2  B=4 T=32768, 30 % reuse: Q and O are 2^31 bytes each (byte offsets up to 2^31 - 1, element
+        offsets past 2^30); rows 0 and 15 (the first and the highest addresses) whole, a
+        2048-token range of every other row.
   cfg3  T=65536, d_qk=192, d_v=128, rule 3: KV head 0 whole, first and last 4096 tokens of the others.
   cfg4  the 16-sequence log-uniform varlen batch (G = 4): every row.
 """
@@ -96,7 +97,7 @@ def test_config1_every_row():
 
 def test_config2_beyond_2gb_offsets():
     w, T, q, *rest = _run("cfg2", seed=2)
-    assert q.numel() * q.element_size() > (1 << 31)
+    assert q.numel() * q.element_size() >= (1 << 31)
     rng = np.random.default_rng(2)
     rows = [(0, 0, T), (w.B * w.Hkv - 1, 0, T)]
     for bkv in range(1, w.B * w.Hkv - 1):
