@@ -394,11 +394,16 @@ def run_ours(args, rank, world, local_rank):
                 sl = (b, slice(kvh * G, (kvh + 1) * G), slice(t0, t1))
                 same &= bool(torch.equal(ho[sl].to(dev).view(torch.int16), o_dev[sl].view(torch.int16)))
         same = reduce_op(0.0 if same else 1.0, world) == 0.0
+        ceil_ms = reduce_op(copy_ceiling(job, rects, (hq, hk, hv, hs), (dq, dk, dv_, ds), (ho, hl), (o, lse),
+                                         args.steps, world), world)
         tok = (w.B * T) if args.scaling == "strong" else (w.B * T * world)
         e2e = {"value": tok / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                "h2d_bytes_per_step": int(reduce_op(float(h2d), world, "sum")),
                "d2h_bytes_per_step": int(reduce_op(float(d2h), world, "sum")), "steps": args.steps,
                "host_result_equals_device": same,
+               "copy_ceiling_ms": ceil_ms, "frac_of_copy_ceiling": ceil_ms / e2e_ms,
+               "copy_ceiling_what": "the same H2D and D2H bytes of every rank, H2D and D2H on two streams at once, "
+                                    "no kernel, max over ranks: the host-link floor of the e2e step",
                "path": "C ABI nsa_sel_run_host: pinned host Q/K/V/sel in, O/LSE out, copies pipelined with the kernel"}
         del hq, hk, hv, hs, ho, hl, dq, dk, dv_, ds, o_dev
 
@@ -447,7 +452,7 @@ def run_ours(args, rank, world, local_rank):
             "traffic": traffic,
             "traffic_source": (f"committed one-pass ncu capture {traffic_src}" if traffic_src else None),
             "dataflow_peak": ceil[1]["gbs"], "dataflow_frac": kv_gbs / ceil[1]["gbs"],
-            "dataflow_what": "the same gather feeding the kernel's 16 UMMAs per chunk (N = 16) from two issuers, "
+            "dataflow_what": "the same gather feeding the kernel's 16 UMMAs per chunk (N = 16) from its three issuers, "
                              "no softmax (libnsa_peaks.so mode 1)",
             "umma_only_gbs": ceil[2]["gbs"],
             "tensor": {"achieved": tf, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": tf / peaks["bf16_tflops"],
@@ -464,6 +469,48 @@ def run_ours(args, rank, world, local_rank):
         "gpu_launches": n_launch,
         "step_ms": step_ms,
     }
+
+
+def copy_ceiling(job, rects, host_in, dev_in, host_out, dev_out, steps, world):
+    """ms per step of the e2e step's host<->device copies alone: for every (batch*KV head) row of
+    this rank's rectangles, its K and V rows and its heads' Q and index rows host->device on one
+    stream while its heads' O and LSE rows go device->host on another (the same bytes the host
+    pipeline moves), with no kernel.  Barrier-bracketed; the caller takes the max over ranks."""
+    import torch
+
+    w, G = job.w, job.G
+    hq, hk, hv, hs = host_in
+    dq, dk, dv, ds = dev_in
+    ho, hl = host_out
+    o, lse = dev_out
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+
+    def one():
+        with torch.cuda.stream(s_in):
+            for b0, b1, t0, t1 in rects:
+                for bkv in range(b0, b1):
+                    b, kvh = divmod(bkv, w.Hkv)
+                    dk[b, kvh].copy_(hk[b, kvh], non_blocking=True)
+                    dv[b, kvh].copy_(hv[b, kvh], non_blocking=True)
+                    ds[b, kvh, t0:t1].copy_(hs[b, kvh, t0:t1], non_blocking=True)
+                    for h in range(kvh * G, (kvh + 1) * G):
+                        dq[b, h, t0:t1].copy_(hq[b, h, t0:t1], non_blocking=True)
+        with torch.cuda.stream(s_out):
+            for b0, b1, t0, t1 in rects:
+                for bkv in range(b0, b1):
+                    b, kvh = divmod(bkv, w.Hkv)
+                    for h in range(kvh * G, (kvh + 1) * G):
+                        ho[b, h, t0:t1].copy_(o[b, h, t0:t1], non_blocking=True)
+                        hl[b, h, t0:t1].copy_(lse[b, h, t0:t1], non_blocking=True)
+
+    one()
+    torch.cuda.synchronize()
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        one()
+    torch.cuda.synchronize()
+    return (time.perf_counter() - t0) * 1e3 / steps
 
 
 def time_gather(o, lse, rects, job, world, stream, reps: int = 3):
@@ -663,7 +710,7 @@ def run_peaks(args):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(0)
     with ClockSampler(0) as clk:
-        res = run_peaks_kernels(dev, reps=max(args.steps, 3))
+        res = run_peaks_kernels(dev, modes=(0, 1, 2, 3, 4), reps=max(args.steps, 3))
     c = clk.summary()
     mhz = c["sm_mhz"] or 1965.0
     for m in res.values():
@@ -671,7 +718,8 @@ def run_peaks(args):
     return {"metric": "on-chip ceilings of the selected-branch dataflow", "value": res[0]["gbs"], "unit": "GB/s",
             "n_gpus": 1, "steps": max(args.steps, 3), "warmup": 1, "higher_is_better": True, "dtype": "bf16",
             "data": "synthetic N(0,1) K/V, pseudo-random 64-key blocks", "config": {"workload": "peaks"},
-            "modes": {"0_gather": res[0], "1_gather_umma": res[1], "2_umma_only": res[2]}, "clocks": c}
+            "modes": {"0_gather": res[0], "1_gather_umma": res[1], "2_umma_only": res[2],
+                      "3_gather_cp_umma": res[3], "4_cp_umma_only": res[4]}, "clocks": c}
 
 
 def run_select(args):

@@ -7,15 +7,19 @@
 // dims, SW128) and two 16 KB V boxes (64 keys x 128 dims), then read by the tensor core as the A
 // operand of 8 score UMMAs (M = 128 keys, N = 16 query rows, K = 16) and 8 PV UMMAs.  The kernels
 // here keep exactly that traffic and drop everything else:
-//   mode 0 (gather): the K and V loader warps run the same rings (3 K stages, 2 V stages of 32 KB)
-//                    and consumers release each stage as soon as it lands: the L2 -> SMEM ceiling
-//                    of this gather;
-//   mode 1 (gather + UMMA): the consumers are two MMA issuers, as in the product kernel: one thread
-//                    issues the chunk's 8 score UMMAs on the landed K tile, another its 8 PV UMMAs on
-//                    the landed V tile, each releasing its stage with tcgen05.commit: the ceiling of
-//                    the whole data path without the softmax and epilogue;
-//   mode 2 (UMMA only): the same two issuers and UMMAs on resident tiles: the tensor-pipe cost of
-//                    one chunk at N = 16.
+//   mode 0 (gather): the K and V loader warps run the same rings (3 K stages; 2 V stages, one per
+//                    PV issuer) and consumers release each stage as soon as it lands: the
+//                    L2 -> SMEM ceiling of this gather;
+//   mode 1 (gather + UMMA): the consumers are the product kernel's three MMA issuers: one thread
+//                    issues every chunk's 8 score UMMAs on the landed K tile, and one thread per
+//                    softmax group (even / odd chunks) issues the chunk's 8 PV UMMAs on its landed V
+//                    stage, each releasing its stage with tcgen05.commit: the ceiling of the whole
+//                    data path without the softmax and epilogue;
+//   mode 2 (UMMA only): the same three issuers and UMMAs on resident tiles: the tensor-pipe cost
+//                    of one chunk at N = 16;
+//   mode 3 / 4:      modes 1 / 2 with the score UMMAs' A operand (the K tile) first copied into
+//                    tensor memory by tcgen05.cp (one 128 x 32 B copy per K = 16 step) and read from
+//                    there by the UMMA: the same bytes leave shared memory once, by the copy engine.
 // Block positions are pseudo-random per (CTA, chunk, sub-block), and all CTAs walk the KV heads
 // in the same order (head = chunk * heads / chunks), as the product kernel's KV-head-major unit
 // order does, so one head's K/V (32 MB) is L2-resident while it is gathered.
@@ -31,11 +35,11 @@ namespace peaks {
 
 using C = nsa::Cfg<128, 128, 16, __nv_bfloat16, 2>;
 constexpr int kKS = 3, kVS = 2;        // ring depths of the product kernel at this shape
-constexpr int kThreads = 128;          // warp 0 K loader, warp 1 V loader, warp 2 score MMA, warp 3 PV MMA
-constexpr int kTmemCols = 32;          // S (16 columns) + O (16 columns)
+constexpr int kThreads = 160;  // warp 0 K loader, 1 V loader, 2 score MMA, 3 / 4 PV MMA of even / odd chunks
+constexpr int kTmemCols = 256;  // S, one O per PV issuer (16 columns each); modes 3-4: two 64-column K tiles at 64
 
 struct Bars {
-  uint64_t k_full[kKS], k_empty[kKS], v_full[kVS], v_empty[kVS], done_s, done_pv;
+  uint64_t k_full[kKS], k_empty[kKS], v_full[kVS], v_empty[kVS], done_s, done_pv[2];
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -96,7 +100,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       nsa::ptx::mbar_init(&bars->v_empty[s], 1);
     }
     nsa::ptx::mbar_init(&bars->done_s, 1);
-    nsa::ptx::mbar_init(&bars->done_pv, 1);
+    nsa::ptx::mbar_init(&bars->done_pv[0], 1);
+    nsa::ptx::mbar_init(&bars->done_pv[1], 1);
     bars->abort_flag = 0;
     nsa::ptx::fence_mbar_init();
   }
@@ -114,7 +119,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = bars->tmem_base;
   const nsa::Waiter w{&bars->abort_flag, p.err, p.timeout_ns};
   const uint64_t pol = nsa::ptx::policy_evict_last();
-  const bool loads = p.mode != 2;
+  const bool loads = p.mode != 2 && p.mode != 4;
+  const bool tmem_a = p.mode >= 3;
 
   if (warp == 0 && loads) {
     // K loader: lane j issues the box of sub-block j / 2, d slice j % 2
@@ -135,20 +141,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) drain_ring(k, bars->k_full, kKS, w);
     __syncwarp();
   } else if (warp == 1 && loads) {
-    nsa::Ring v;
+    // V loader: chunk c goes to stage c % 2, the stage of the PV issuer of c's softmax group
     for (int c = 0; c < p.n_chunks; ++c) {
+      const int vs = c & 1;
+      const uint32_t use = (uint32_t)c >> 1;
       int go = 1;
       if (lane == 0) {
-        go = (!v.lapped || w.wait(&bars->v_empty[v.idx], v.phase ^ 1u)) ? 1 : 0;
-        if (go) nsa::ptx::mbar_arrive_expect_tx(&bars->v_full[v.idx], (uint32_t)C::kVStage);
+        go = (use == 0 || w.wait(&bars->v_empty[vs], (use - 1u) & 1u)) ? 1 : 0;
+        if (go) nsa::ptx::mbar_arrive_expect_tx(&bars->v_full[vs], (uint32_t)C::kVStage);
       }
       if (!__shfl_sync(0xffffffffu, go, 0)) break;
       if (lane < 2)
-        nsa::ptx::tma_load_4d(smem + kOffV + v.idx * C::kVStage + lane * C::kVSub, &tmV, &bars->v_full[v.idx], 0,
+        nsa::ptx::tma_load_4d(smem + kOffV + vs * C::kVStage + lane * C::kVSub, &tmV, &bars->v_full[vs], 0,
                               block_row(p, c, lane), 0, head_of(p, c), pol);
-      v.next(kVS);
     }
-    if (lane == 0) drain_ring(v, bars->v_full, kVS, w);
+    if (lane == 0) {  // the most recent load of each stage has landed
+      for (int vs = 0; vs < 2; ++vs) {
+        const int last = p.n_chunks - 1 - ((p.n_chunks - 1 - vs) & 1);  // last chunk with parity vs
+        if (last >= 0 && (last & 1) == vs) w.wait_drain(&bars->v_full[vs], ((uint32_t)last >> 1) & 1u);
+      }
+    }
     __syncwarp();
   } else if (warp == 2 && lane == 0) {
     // score issuer: S^T[128 keys x 16] = K_chunk . Q^T into TMEM columns 0-15
@@ -162,10 +174,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else {
         nsa::ptx::tc_fence_after();
         const uint64_t a0 = nsa::ptx::sdesc_sw128(k_base + k.idx * C::kKStage, 16, 1024);
+        if (tmem_a) {
+          const uint32_t ta = tmem + 64 + 64 * (uint32_t)(c & 1);
 #pragma unroll
-        for (int j = 0; j < C::DQK / 16; ++j)
-          nsa::ptx::umma_bf16(tmem, nsa::desc_add(a0, (j >> 2) * C::kKChunkStride + (j & 3) * 32),
-                              nsa::desc_add(bq0, (j >> 2) * C::kQChunk + (j & 3) * 32), C::kIdescS, j > 0 ? 1u : 0u);
+          for (int j = 0; j < C::DQK / 16; ++j)
+            nsa::ptx::tmem_cp_128x256b(ta + 8 * j, nsa::desc_add(a0, (j >> 2) * C::kKChunkStride + (j & 3) * 32));
+#pragma unroll
+          for (int j = 0; j < C::DQK / 16; ++j)
+            nsa::ptx::umma_bf16_ts(tmem, ta + 8 * j, nsa::desc_add(bq0, (j >> 2) * C::kQChunk + (j & 3) * 32),
+                                   C::kIdescS, j > 0 ? 1u : 0u);
+        } else {
+#pragma unroll
+          for (int j = 0; j < C::DQK / 16; ++j)
+            nsa::ptx::umma_bf16(tmem, nsa::desc_add(a0, (j >> 2) * C::kKChunkStride + (j & 3) * 32),
+                                nsa::desc_add(bq0, (j >> 2) * C::kQChunk + (j & 3) * 32), C::kIdescS, j > 0 ? 1u : 0u);
+        }
         if (loads) nsa::ptx::umma_commit(&bars->k_empty[k.idx]);
       }
       k.next(kKS);
@@ -173,28 +196,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     // every UMMA issued by this thread completes before TMEM is released
     nsa::ptx::umma_commit(&bars->done_s);
     w.wait_drain(&bars->done_s, 0);
-  } else if (warp == 3 && lane == 0) {
-    // PV issuer: O^T[128 dims x 16] += V_chunk^T . P^T into TMEM columns 16-31
-    const uint32_t v_base = nsa::ptx::smem_u32(smem + kOffV);
+  } else if ((warp == 3 || warp == 4) && lane == 0) {
+    // PV issuer of softmax group g (chunks c % 2 == g): O^T[128 dims x 16] += V_chunk^T . P^T
+    const int g = warp - 3;
+    const uint32_t v_base = nsa::ptx::smem_u32(smem + kOffV + g * C::kVStage);
     const uint64_t bp0 = nsa::ptx::sdesc_sw128(nsa::ptx::smem_u32(smem + kOffP), 16, 1024);
-    nsa::Ring v;
-    for (int c = 0; c < p.n_chunks; ++c) {
-      if (loads && !w.wait(&bars->v_full[v.idx], v.phase)) break;
+    for (int c = g; c < p.n_chunks; c += 2) {
+      const uint32_t use = (uint32_t)c >> 1;
+      if (loads && !w.wait(&bars->v_full[g], use & 1u)) break;
       if (p.mode == 0) {
-        nsa::ptx::mbar_arrive(&bars->v_empty[v.idx]);
+        nsa::ptx::mbar_arrive(&bars->v_empty[g]);
       } else {
         nsa::ptx::tc_fence_after();
-        const uint64_t a0 = nsa::ptx::sdesc_sw128(v_base + v.idx * C::kVStage, C::kBox, 1024);
+        const uint64_t a0 = nsa::ptx::sdesc_sw128(v_base, C::kBox, 1024);
 #pragma unroll
         for (int j = 0; j < 8; ++j)
-          nsa::ptx::umma_bf16(tmem + 16, nsa::desc_add(a0, (j >> 2) * C::kVSub + (j & 3) * 2048),
+          nsa::ptx::umma_bf16(tmem + 16 + 16 * g, nsa::desc_add(a0, (j >> 2) * C::kVSub + (j & 3) * 2048),
                               nsa::desc_add(bp0, (j >> 2) * C::kPSub + (j & 3) * 32), C::kIdescPV, 1u);
-        if (loads) nsa::ptx::umma_commit(&bars->v_empty[v.idx]);
+        if (loads) nsa::ptx::umma_commit(&bars->v_empty[g]);
       }
-      v.next(kVS);
     }
-    nsa::ptx::umma_commit(&bars->done_pv);
-    w.wait_drain(&bars->done_pv, 0);
+    nsa::ptx::umma_commit(&bars->done_pv[g]);
+    w.wait_drain(&bars->done_pv[g], 0);
   }
   nsa::ptx::tc_fence_before();
   __syncthreads();
@@ -220,14 +243,14 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 extern "C" {
 
-// Launch one microbenchmark (mode 0, 1 or 2, see above) on `stream` over K, V bf16
+// Launch one microbenchmark (mode 0 to 4, see above) on `stream` over K, V bf16
 // [n_heads, T, 128] with `ctas` CTAs (one per SM) of `n_chunks` 128-key chunks each.  Returns 0,
 // or a negative code with a message on stderr.  `err` (device int32, optional) receives the
-// bounded-wait timeout bit.  Bytes gathered per launch (modes 0 and 1): ctas * n_chunks * 64 KB.
+// bounded-wait timeout bit.  Bytes gathered per launch (modes 0, 1, 3): ctas * n_chunks * 64 KB.
 int nsa_peaks_run(const void* k, const void* v, int n_heads, int T, int n_chunks, int mode, int ctas, int32_t* err,
                   cudaStream_t stream) {
   if (k == nullptr || v == nullptr || n_heads <= 0 || T < 128 || T % 64 != 0 || n_chunks <= 0 || ctas <= 0 ||
-      mode < 0 || mode > 2) {
+      mode < 0 || mode > 4) {
     fprintf(stderr, "nsa_peaks_run: bad arguments\n");
     return -1;
   }

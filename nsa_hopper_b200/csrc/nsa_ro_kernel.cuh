@@ -234,6 +234,10 @@ __device__ void softmax_role_ro(const Params& p, uint8_t* smem, SmemBars* bars, 
   float* lsum1 = reinterpret_cast<float*>(smem + p.off_fac);   // [row]
   const float sl2 = p.scale_log2;
   const int ci = r - (r / p.BQs) * p.BQs;                   // token of the row inside the unit
+  // A 64-row tile (G * BQs = 64) leaves rows 64-127 as zero query padding: their scores are exactly
+  // 0 and the PV MMA reads those unrewritten score columns as P = 0, so the two warps of each group
+  // that own only padding rows skip the exp pass and the P stores (half the exp work of the mode).
+  const bool pad = quarter * 32 >= p.G * p.BQs;
   uint32_t ui = 0, ne = 0, kc = 0;
   bool dead = false;
 
@@ -264,6 +268,12 @@ __device__ void softmax_role_ro(const Params& p, uint8_t* smem, SmemBars* bars, 
 
     for (int c = 0; c < nch; ++c, ++kc) {
       const int sl = (int)(kc & 1u);
+      if (pad) {  // only the row-max barrier and the P-ready arrival
+        ptx::named_bar_sync(kWgBar0, 256);
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&bars->p_full[sl]);
+        continue;
+      }
       dead |= !w.wait_inline(&bars->s_full[sl], (kc >> 1) & 1u);
       ptx::tc_fence_after();
       const uint32_t sbase = tmem + lane_addr + C::kTmemS + sl * 128 + 64 * h;
@@ -293,6 +303,7 @@ __device__ void softmax_role_ro(const Params& p, uint8_t* smem, SmemBars* bars, 
       ptx::named_bar_sync(kWgBar0, 256);
       const float cmax_x = fmaxf(xm[r], xm[128 + r]) * sl2;
       float m_use = m_run, alpha = 1.f;
+      bool need = false;
       if (first) {
         m_use = cmax_x;
       } else {
@@ -300,22 +311,27 @@ __device__ void softmax_role_ro(const Params& p, uint8_t* smem, SmemBars* bars, 
         if (m_cand > m_run + kRescaleLog2) {
           alpha = (m_run == -INFINITY) ? 0.f : ptx::ex2(m_run - m_cand);
           m_use = m_cand;
-          if (h == 0) {
-            // this row's O, once the PV of the previous chunk (which released its buffer) is done
-            dead |= !w.wait_inline(&bars->s_empty[(kc - 1) & 1u], ((kc - 1) >> 1) & 1u);
-            ptx::tc_fence_after();
-#pragma unroll
-            for (int h0 = 0; h0 < C::DV; h0 += 16) {
-              float o[16];
-              ptx::tmem_ld16(obase + h0, o);
-              ptx::tmem_wait_ld();
-#pragma unroll
-              for (int j = 0; j < 16; ++j) o[j] *= alpha;
-              ptx::tmem_st16(obase + h0, o);
-            }
-            ptx::tmem_wait_st();
-          }
+          need = true;
         }
+      }
+      // Rescale O in group 0.  The decision is per row, but tcgen05.ld / tcgen05.st are
+      // .sync.aligned (the whole warp executes them together), so a warp with any row to rescale
+      // runs the pass for all its lanes, the others with alpha = 1.  (A lane-divergent pass here
+      // stalled the warp: rows whose running max jumped by more than 2^8 next to rows whose did not.)
+      if (h == 0 && __any_sync(0xffffffffu, need)) {
+        // the rows' O, once the PV of the previous chunk (which released its buffer) is done
+        dead |= !w.wait_inline(&bars->s_empty[(kc - 1) & 1u], ((kc - 1) >> 1) & 1u);
+        ptx::tc_fence_after();
+#pragma unroll
+        for (int h0 = 0; h0 < C::DV; h0 += 16) {
+          float o[16];
+          ptx::tmem_ld16(obase + h0, o);
+          ptx::tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) o[j] *= alpha;
+          ptx::tmem_st16(obase + h0, o);
+        }
+        ptx::tmem_wait_st();
       }
 
       // pass 2: exp2, the partial row sum, and P as bf16 pairs in columns [64h, 64h + 32) of the

@@ -111,3 +111,24 @@ def test_nsa_forward_fused_gate_equals_branch_sum(T):
     want = g[0] * o_cmp + g[1] * o_sel + g[2] * o_win
     torch.cuda.synchronize()
     assert (o - want).abs().max().item() <= 1e-5 * max(1.0, want.abs().max().item())
+
+
+def test_row_owner_rescale_of_one_row_in_a_warp():
+    """A lazy O rescale that only some rows of a warp need (the row-owner kernel's tensor-memory
+    pass runs warp-wide).  G = 1 with 128-token tiles and window 128: row t = 128 of its tile sees
+    only key 128 in its first chunk; that key gets a very low score for it, so the row's running
+    max jumps by far more than 2^8 at the next chunk while its neighbours' do not."""
+    B, H, T, D, window = 1, 1, 512, 64, 128
+    g = torch.Generator(device="cuda").manual_seed(77)
+    q = torch.randn(B, H, T, D, device="cuda", generator=g)
+    k = torch.randn(B, H, T, D, device="cuda", generator=g)
+    v = torch.randn(B, H, T, D, device="cuda", generator=g)
+    k[:, :, 128] = -8.0 * q[:, :, 128]
+    q, k, v = (x.to(torch.bfloat16) for x in (q, k, v))
+    bq = nsa.branch_q_block(1)
+    assert bq == 128
+    sel = nsa.window_selection(B, H, T, window, 64, q.device, bq)
+    o, _ = ops.forward_ext(q, k, v, sel, 64, bq, window=window, key_map=0)
+    ref = nsa.window_branch(q, k, v, window)
+    torch.cuda.synchronize()
+    assert (o - ref).abs().max().item() <= 2e-2
