@@ -184,9 +184,13 @@ int nsa_sel_plan(const nsa_sel_desc* desc, int32_t sm_count, nsa_sel_plan_info* 
        sel_out int32 [B, Hkv, T, k],  k = min(n_sel, ceil(T / l_prime)) <= 32,
    the k best visible blocks (nb * l_prime <= t) by score, highest first; -1 where fewer than k
    blocks are visible (the reference's topk returns masked future blocks there, which the
-   selected branch ignores in the same way).  Scores are fp32.  q, k bf16 as in nsa_sel_forward
-   (d_qk = d, d % 8 == 0, d <= 256; q 16-byte aligned); kblk_workspace: caller-owned fp32 buffer of nsa_sel_select_workspace_bytes()
-   bytes, 16-byte aligned.  Two kernel launches on `stream`. */
+   selected branch ignores in the same way).  q, k bf16 as in nsa_sel_forward (d_qk = d,
+   d % 8 == 0, d <= 256; q 16-byte aligned); kblk_workspace: caller-owned buffer of
+   nsa_sel_select_workspace_bytes() bytes, 16-byte aligned.  Two kernel launches on `stream`.
+   For d = 64 and 128 the scores run on the tensor cores with each operand split into two bf16
+   parts (hi + lo, three products accumulated in fp32: about 16 bits of each operand, ranking
+   equal to fp32 scores except at near-ties); other d use fp32 FMA.  The tensor-core kernel's
+   in-kernel waits are bounded; nsa_sel_select_status() reports one that ran out. */
 int nsa_sel_select(const void* q, const void* k, float* kblk_workspace, int32_t* sel_out, int32_t B, int32_t Hq,
                    int32_t Hkv, int32_t T, int32_t d, int32_t l_prime, int32_t n_sel, int32_t cmp_block,
                    int32_t cmp_stride, nsa_stream_t stream);
@@ -207,6 +211,11 @@ int nsa_sel_select_noalloc(const void* q, const void* k, int32_t* sel_out, int32
 
 /* Size in bytes of the static scratch used by nsa_sel_select_noalloc. */
 int64_t nsa_sel_select_static_scratch_bytes(void);
+
+/* NSA_DEVERR_* bits that selection launches on the current device set since the last call (0 =
+   none), cleared on return; -1 if the device cannot be queried.  Synchronous: it waits for the
+   device's pending work through a blocking copy. */
+int32_t nsa_sel_select_status(void);
 
 /* Text of the last error on this host thread ("" if none). */
 const char* nsa_sel_last_error(void);

@@ -120,6 +120,8 @@ def load(path: Optional[str] = None) -> ctypes.CDLL:
     lib.nsa_sel_select_noalloc.restype = ctypes.c_int
     lib.nsa_sel_select_static_scratch_bytes.argtypes = []
     lib.nsa_sel_select_static_scratch_bytes.restype = ctypes.c_int64
+    lib.nsa_sel_select_status.argtypes = []
+    lib.nsa_sel_select_status.restype = ctypes.c_int32
     if path is None:
         _lib = lib
     return lib
@@ -178,6 +180,11 @@ def select_noalloc(q: int, k: int, sel_out: int, B: int, Hq: int, Hkv: int, T: i
     """nsa_sel_select_noalloc: block selection with the library's static scratch (no allocation)."""
     check(load().nsa_sel_select_noalloc(ctypes.c_void_p(q), ctypes.c_void_p(k), ctypes.c_void_p(sel_out), B, Hq,
                                         Hkv, T, d, l_prime, n_sel, cmp_block, cmp_stride, ctypes.c_void_p(stream)))
+
+
+def select_status() -> int:
+    """nsa_sel_select_status: device error bits of the selection launches so far (then cleared)."""
+    return int(load().nsa_sel_select_status())
 
 
 def make_host_io(**kw) -> NsaSelHostIO:

@@ -21,6 +21,7 @@
 #include "nsa_sel_kernel.cuh"
 #include "nsa_ro_kernel.cuh"
 #include "nsa_select_kernel.cuh"
+#include "nsa_select_tc_kernel.cuh"
 
 namespace {
 
@@ -521,6 +522,9 @@ int launch(const nsa_sel_desc* d, nsa_stream_t stream) {
 // block-key table lives in this module-scope device array, so the call never allocates.
 constexpr size_t kStaticSelectScratchFloats = (size_t)4 << 20;  // 16 MB
 __device__ __align__(256) float g_select_scratch[kStaticSelectScratchFloats];
+// Device error word of the tensor-core selection kernel (NSA_DEVERR_* bits; read and cleared by
+// nsa_sel_select_status).  Static device memory, resolved per device like the others.
+__device__ int32_t g_select_err;
 
 namespace {
 float* g_select_scratch_ptr[kMaxDevices] = {};
@@ -536,6 +540,20 @@ int static_select_scratch(int dev, float** out) {
     g_select_scratch_ptr[dev] = static_cast<float*>(ptr);
   }
   *out = g_select_scratch_ptr[dev];
+  return NSA_OK;
+}
+
+int32_t* g_select_err_ptr[kMaxDevices] = {};
+
+int select_err_word(int dev, int32_t** out) {
+  std::lock_guard<std::mutex> lk(g_dev.mu);
+  if (g_select_err_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_select_err);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(selection error word)");
+    g_select_err_ptr[dev] = static_cast<int32_t*>(ptr);
+  }
+  *out = g_select_err_ptr[dev];
   return NSA_OK;
 }
 
@@ -555,6 +573,77 @@ int select_shape(int32_t B, int32_t Hq, int32_t Hkv, int32_t T, int32_t d, int32
   if (*topk > nsa::select::kMaxK) return fail(NSA_ERR_UNSUPPORTED, "top-k of %d exceeds %d", *topk, nsa::select::kMaxK);
   *n_cmp = T >= cmp_block ? (T - cmp_block) / cmp_stride + 1 : 0;
   return NSA_OK;
+}
+
+// The tensor-core selection (d = 64 or 128): the split block-key table, then select_tc_kernel.
+template <int D, int K>
+int select_tc_launch(const void* q, float* ws, int32_t* sel, int B, int Hq, int Hkv, int T, int l_prime, int topk,
+                     int n_blk, int sm, int dev, cudaStream_t st) {
+  CUtensorMap tmB;
+  {
+    // [part (hi, lo)][b*Hkv][n_blk][D] bf16; one box = 64 dims x 128 blocks (SW128)
+    const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)n_blk, (cuuint64_t)B * Hkv, 2};
+    const cuuint64_t str[3] = {(cuuint64_t)D * 2, (cuuint64_t)D * 2 * n_blk, (cuuint64_t)D * 2 * n_blk * B * Hkv};
+    const cuuint32_t box[4] = {64, (cuuint32_t)nsa::seltc::kNT, 1, 1};
+    int rc = encode(&tmB, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, ws, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "block keys");
+    if (rc != NSA_OK) return rc;
+  }
+  int32_t* err = nullptr;
+  int rc = select_err_word(dev, &err);
+  if (rc != NSA_OK) return rc;
+  nsa::seltc::Params p{};
+  p.q = static_cast<const bf16*>(q);
+  p.sel = sel;
+  p.err = err;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.T = T;
+  p.G = Hq / Hkv;
+  p.n_blk = n_blk;
+  p.l_prime = l_prime;
+  p.topk = topk;
+  p.n_tiles = (T + nsa::seltc::kRows - 1) / nsa::seltc::kRows;
+  p.n_units = B * Hkv * p.n_tiles;
+  const char* e = getenv("NSA_SEL_TIMEOUT_MS");
+  const int tmo = e ? atoi(e) : 0;
+  p.timeout_ns = (unsigned long long)(tmo > 0 ? tmo : 2000) * 1000000ull;
+  const uint32_t smem = nsa::seltc::smem_bytes<D>();
+  {
+    std::lock_guard<std::mutex> lk(g_dev.mu);
+    const uint64_t bit = 1ull << (59 + (D == 64 ? 0 : 2) + (K == 16 ? 0 : 1));
+    if ((g_dev.attr_done[dev] & bit) == 0) {
+      cudaError_t ae = cudaFuncSetAttribute(reinterpret_cast<const void*>(&nsa::seltc::select_tc_kernel<D, K>),
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (ae != cudaSuccess) return cuda_fail(ae, "cudaFuncSetAttribute(tensor-core selection smem)");
+      g_dev.attr_done[dev] |= bit;
+    }
+  }
+  const int grid = p.n_units < sm ? p.n_units : sm;
+  void* args[] = {&tmB, &p};
+  cudaError_t le = cudaLaunchKernel(reinterpret_cast<const void*>(&nsa::seltc::select_tc_kernel<D, K>), dim3(grid),
+                                    dim3(nsa::seltc::kThreads), args, smem, st);
+  if (le != cudaSuccess) return cuda_fail(le, "tensor-core selection kernel launch");
+  return NSA_OK;
+}
+
+int select_tc(const void* q, const void* k, float* ws, int32_t* sel, int B, int Hq, int Hkv, int T, int d,
+              int l_prime, int topk, int n_blk, int n_cmp, int cmp_block, int cmp_stride, float scale, int sm, int dev,
+              cudaStream_t st) {
+  nsa::select::kblk_kernel<true><<<dim3(n_blk, B * Hkv), d, 0, st>>>(static_cast<const bf16*>(k), ws, T, d, n_blk,
+                                                                      n_cmp, l_prime, cmp_block, cmp_stride, scale);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "block-key kernel launch");
+  // list capacity: 16 when k <= 16 (the BASELINE top-16), else 32
+  int rc;
+  if (d == 64)
+    rc = topk <= 16 ? select_tc_launch<64, 16>(q, ws, sel, B, Hq, Hkv, T, l_prime, topk, n_blk, sm, dev, st)
+                    : select_tc_launch<64, 32>(q, ws, sel, B, Hq, Hkv, T, l_prime, topk, n_blk, sm, dev, st);
+  else
+    rc = topk <= 16 ? select_tc_launch<128, 16>(q, ws, sel, B, Hq, Hkv, T, l_prime, topk, n_blk, sm, dev, st)
+                    : select_tc_launch<128, 32>(q, ws, sel, B, Hq, Hkv, T, l_prime, topk, n_blk, sm, dev, st);
+  if (rc == NSA_OK) g_last_error[0] = '\0';
+  return rc;
 }
 
 // ------------------------------------------------------------------ host-buffer pipeline
@@ -712,6 +801,10 @@ int nsa_sel_select(const void* q, const void* k, float* kblk_workspace, int32_t*
   int sm = 0, dev = 0;
   rc = current_sm_count(&sm, &dev);
   if (rc != NSA_OK) return rc;
+  const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const float scale = (float)(1.0 / ((double)cmp_block * sqrt((double)d)));
+  if (d == 64 || d == 128) return select_tc(q, k, kblk_workspace, sel_out, B, Hq, Hkv, T, d, l_prime, topk, n_blk,
+                                            n_cmp, cmp_block, cmp_stride, scale, sm, dev, st);
   const int smem = (2 * nsa::select::kTile * (d + 4) + nsa::select::kTile * (nsa::select::kChunk + 1)) * 4;
   {
     std::lock_guard<std::mutex> lk(g_dev.mu);
@@ -725,9 +818,7 @@ int nsa_sel_select(const void* q, const void* k, float* kblk_workspace, int32_t*
       g_dev.attr_done[dev] |= bit;
     }
   }
-  const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const float scale = (float)(1.0 / ((double)cmp_block * sqrt((double)d)));
-  nsa::select::kblk_kernel<<<dim3(n_blk, B * Hkv), d, 0, st>>>(static_cast<const bf16*>(k), kblk_workspace, T, d,
+  nsa::select::kblk_kernel<false><<<dim3(n_blk, B * Hkv), d, 0, st>>>(static_cast<const bf16*>(k), kblk_workspace, T, d,
                                                                n_blk, n_cmp, l_prime, cmp_block, cmp_stride, scale);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "block-key kernel launch");
@@ -760,6 +851,18 @@ int nsa_sel_select_noalloc(const void* q, const void* k, int32_t* sel_out, int32
 }
 
 int64_t nsa_sel_select_static_scratch_bytes(void) { return (int64_t)(kStaticSelectScratchFloats * sizeof(float)); }
+
+int32_t nsa_sel_select_status(void) {
+  int sm = 0, dev = 0;
+  if (current_sm_count(&sm, &dev) != NSA_OK) return -1;
+  int32_t* w = nullptr;
+  if (select_err_word(dev, &w) != NSA_OK) return -1;
+  int32_t v = 0;
+  if (cudaMemcpy(&v, w, sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+  const int32_t zero = 0;
+  if (cudaMemcpy(w, &zero, sizeof(zero), cudaMemcpyHostToDevice) != cudaSuccess) return -1;
+  return v;
+}
 
 int nsa_sel_run(const nsa_sel_desc* desc, nsa_stream_t stream) { return launch(desc, stream); }
 

@@ -44,6 +44,10 @@ __device__ __forceinline__ int cmp_block_of(int i, int T, int n_cmp, int l_prime
 
 // kblk[bh, nb, :] = scale * sum over compressed keys i of block nb of sum_j k[bh, i*stride + j, :]
 // (scale = 1 / (cmp_block * sqrt(d))).  One CTA per (block, b*Hkv), one thread per dimension.
+// SPLIT = false: an fp32 table [B*Hkv, n_blk, d].  SPLIT = true: the same bytes hold two bf16
+// tables [2][B*Hkv, n_blk, d], hi = bf16(x) and lo = bf16(x - hi), the tensor-core operands of
+// select_tc_kernel (nsa_select_tc_kernel.cuh).
+template <bool SPLIT>
 __global__ void kblk_kernel(const __nv_bfloat16* __restrict__ k, float* __restrict__ kblk, int T, int d, int n_blk,
                             int n_cmp, int l_prime, int cmp_block, int cmp_stride, float scale) {
   const int nb = blockIdx.x, bh = blockIdx.y, dd = threadIdx.x;
@@ -65,7 +69,16 @@ __global__ void kblk_kernel(const __nv_bfloat16* __restrict__ k, float* __restri
     for (int j = 0; j < cmp_block; ++j) w += __bfloat162float(kb[(size_t)(r0 + j) * d]);
     acc += w;
   }
-  kblk[((size_t)bh * n_blk + nb) * d + dd] = acc * scale;
+  const size_t at = ((size_t)bh * n_blk + nb) * d + dd;
+  if constexpr (SPLIT) {
+    const float x = acc * scale;
+    const __nv_bfloat16 hi = __float2bfloat16_rn(x);
+    __nv_bfloat16* tab = reinterpret_cast<__nv_bfloat16*>(kblk);
+    tab[at] = hi;
+    tab[(size_t)gridDim.y * n_blk * d + at] = __float2bfloat16_rn(x - __bfloat162float(hi));
+  } else {
+    kblk[at] = acc * scale;
+  }
 }
 
 // Ranking of (score, block) pairs: higher score first, ties by smaller block index.
