@@ -107,24 +107,11 @@ __device__ void producer_role(const Params& p, uint8_t* smem, Bars* bars, const 
   // loads: 4 lanes per row (16 bytes = 8 dims each), 8 rows per instruction, so every warp-wide
   // load reads eight whole 64-byte row segments
   const int lrow = lane >> 2, lpart = lane & 3;
-  // The query rows of the unit after next (per head, 128 tokens x D dims: one contiguous range)
-  // are prefetched into L2 while this unit's are summed.
-  auto prefetch_unit = [&](int u) {
-    if (u >= p.n_units || threadIdx.x >= (unsigned)p.G) return;
-    const int bkv = u / p.n_tiles, t0 = (u - bkv * p.n_tiles) * kRows;
-    const int b = bkv / p.Hkv, kvh = bkv - b * p.Hkv;
-    const int rows = min(kRows, p.T - t0);
-    ptx::prefetch_l2_bulk(p.q + (((size_t)b * p.Hq + (size_t)kvh * p.G + threadIdx.x) * p.T + t0) * D,
-                          (uint32_t)rows * D * 2);
-  };
-  prefetch_unit(blockIdx.x);
-  prefetch_unit(blockIdx.x + gridDim.x);
   int li = 0;
   for (int u = blockIdx.x; u < p.n_units; u += gridDim.x, ++li) {
     const int bkv = u / p.n_tiles, t0 = (u - bkv * p.n_tiles) * kRows;
     const int b = bkv / p.Hkv, kvh = bkv - b * p.Hkv;
     const int ab = li & 1;
-    prefetch_unit(u + 2 * gridDim.x);  // two units ahead
     if (li >= 2 && !w.wait(&bars->a_empty[ab], ((li >> 1) - 1) & 1)) break;
     ptx::tc_fence_after();
     const uint32_t abase = tmem + lane_addr + C::kTmemA + (uint32_t)ab * 2 * C::kACols;
