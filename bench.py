@@ -75,27 +75,90 @@ def committed_traffic(workload: str):
 
 
 class ClockSampler:
-    """nvidia-smi clock/throttle sampling while the timed region runs."""
+    """SM clock and throttle-reason sampling while the timed region runs.  NVML is read every
+    10 ms from a thread that has taken its first sample before the region starts, so even a
+    100 ms region gets about ten samples; where NVML cannot be loaded, nvidia-smi is polled
+    every 200 ms instead.  Only reads: no clock or other GPU setting is touched."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits (nvml.h nvmlClocksEventReason*)
+    REASON_BITS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+                   ("sw_power_cap", 0x4))
 
-    def __init__(self, gpu_index: int):
+    def __init__(self, gpu_index: int, period_s: float = 0.01):
         self.gpu = gpu_index
+        self.period = period_s
         self.proc = None
         self.out = ""
+        self.samples = []  # (sm MHz, max sm MHz, reason names)
+        self.source = None
+        self._thread = None
+        self._stop = None
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        try:
+            pr = torch.cuda.get_device_properties(self.gpu)
+            bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+
+    def _poll(self, nv, h, first):
+        while True:
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+            except Exception:
+                first.set()
+                return
+            self.samples.append((float(sm), float(mx), [n for n, b in self.REASON_BITS if bits & b]))
+            first.set()
+            if self._stop.wait(self.period):
+                return
 
     def __enter__(self):
+        import threading
+
+        try:
+            nv, h = self._nvml_handle()
+            self._stop, first = threading.Event(), threading.Event()
+            self._thread = threading.Thread(target=self._poll, args=(nv, h, first), daemon=True)
+            self._thread.start()
+            first.wait(2.0)
+            if self.samples:
+                self.source = f"nvml every {int(self.period * 1000)} ms"
+                return self
+            self._stop.set()
+            self._thread.join(timeout=2.0)
+            self._thread = None
+        except Exception:
+            self._thread = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.source = "nvidia-smi every 200 ms"
         except Exception:
             self.proc = None
         return self
 
     def __exit__(self, *a):
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=2.0)
+            try:
+                import pynvml
+
+                pynvml.nvmlShutdown()
+            except Exception:
+                pass
         if self.proc is not None:
             time.sleep(0.25)
             self.proc.terminate()
@@ -107,7 +170,11 @@ class ClockSampler:
 
     def summary(self):
         sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for a, b, r in self.samples:
+            sm.append(a)
+            mx.append(b)
+            reasons.update(r)
+        names = [n for n, _ in self.REASON_BITS]
         for line in (self.out or "").splitlines():
             f = [x.strip() for x in line.split(",")]
             if len(f) < 9:
@@ -121,9 +188,9 @@ class ClockSampler:
                 if val.lower().startswith("active"):
                     reasons.add(n)
         if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "source": self.source}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": self.source}
 
 
 def reduce_op(x: float, world: int, op: str = "max") -> float:
@@ -725,9 +792,11 @@ def run_peaks(args):
 def run_select(args):
     """--stage select: the block-selection kernel (nsa_sel_select) on the workload's shapes.
     Algorithmic work per (b, kvh, token t): the group sum of G query rows (G*d adds) and one
-    d-long fp32 dot product per visible block (t // l_prime + 1 of them); bytes: Q (bf16) in,
-    k int32 indices out.  The scores run on the fp32 CUDA cores, so the roofline is the nominal
-    fp32 FMA peak (no measured figure exists for it on this pool)."""
+    d-long dot product per visible block (t // l_prime + 1 of them); bytes: Q (bf16) in, k int32
+    indices out.  For d = 64 and 128 the scores run on the tensor cores as three bf16 products
+    (hi*hi + hi*lo + lo*hi), so the roofline counts 3 * 2 * d flops per visible (token, block)
+    against the measured bf16 peak; other d run on the fp32 CUDA cores against the nominal fp32
+    FMA peak (no measured figure exists for it on this pool)."""
     import torch
 
     from nsa_hopper_b200 import capi, workload
@@ -765,17 +834,27 @@ def run_select(args):
         torch.cuda.synchronize()
     ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
     t = np.arange(T, dtype=np.float64)
-    flops = B * Hkv * float(((t // lp + 1) * 2 * D).sum() + T * G * D)
+    pairs = B * Hkv * float((t // lp + 1).sum())
+    tensor = D in (64, 128)
+    if tensor:
+        pk = measured_peaks()
+        flops = pairs * 3 * 2 * D
+        peak, bound = pk["bf16_tflops"], "tensor"
+        peak_kind = f"{pk['kind']} (MEASURED_PEAKS.json bf16_tflops, burst)"
+    else:
+        flops = pairs * 2 * D + B * Hkv * float(T * G * D)
+        peak, bound, peak_kind = FP32_FMA_PEAK_TFLOPS, "fp32", "nominal"
     byts = B * Hkv * T * (G * D * 2 + kk * 4)
     achieved = flops / (ms * 1e-3) / 1e12
     return {
         "metric": "block selection (scores + top-k) tokens/s", "value": B * T / (ms * 1e-3), "unit": "tokens/s",
         "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (bf16 inputs)", "data": "synthetic N(0,1) bf16 Q/K",
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16 hi/lo split, fp32 accumulate" if tensor else "fp32 (bf16 inputs)",
+        "data": "synthetic N(0,1) bf16 Q/K",
         "config": {"workload": args.config, "stage": "select", "B": B, "T": T, "Hq": Hq, "Hkv": Hkv, "d": D,
                    "block": lp, "top_n": n, "l2": "256 MiB buffer written between timed steps (L2 flushed)"},
-        "roofline": {"bound": "fp32", "achieved": achieved, "peak": FP32_FMA_PEAK_TFLOPS, "unit": "TFLOP/s",
-                     "frac": achieved / FP32_FMA_PEAK_TFLOPS, "traffic": None, "peak_kind": "nominal",
+        "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind,
                      "algorithmic_flops_per_launch": flops, "algorithmic_bytes_per_launch": byts,
                      "hbm_gbs": byts / (ms * 1e-3) / 1e9},
         "e2e": None, "clocks": clk.summary(), "gpu_launches": 2 * args.steps, "cpu_baseline": None,

@@ -63,9 +63,12 @@ typedef struct CUstream_st* nsa_stream_t;
    the bounded-wait error path (NSA_DEVERR_TIMEOUT after timeout_ms) without any fault. */
 #define NSA_DEBUG_STALL 1
 /* Comparison switches (same results, different schedule): hand out work units in fixed strides
-   instead of from the dynamic counter; never use the row-owner kernel for 64/128-row tiles. */
+   instead of from the dynamic counter; never use the row-owner kernel for 64/128-row tiles; run a
+   64-row tile of the row-owner kernel as 128-row MMAs with 64 rows of zero padding instead of
+   M = 64 MMAs. */
 #define NSA_DEBUG_STATIC_UNITS 2
 #define NSA_DEBUG_NO_ROW_OWNER 4
+#define NSA_DEBUG_RO_PAD128 8
 
 #define NSA_DTYPE_BF16 0
 #define NSA_DTYPE_F32 1

@@ -27,6 +27,7 @@ NSA_DEVERR_TIMEOUT = 1
 NSA_DEBUG_STALL = 1
 NSA_DEBUG_STATIC_UNITS = 2
 NSA_DEBUG_NO_ROW_OWNER = 4
+NSA_DEBUG_RO_PAD128 = 8
 DTYPE_BF16 = 0
 DTYPE_F32 = 1
 KEYMAP_CAUSAL = 0

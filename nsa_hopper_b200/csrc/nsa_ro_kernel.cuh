@@ -1,5 +1,5 @@
-// Row-owner forward for 128-row query tiles (G heads x 128/G tokens sharing one selection row;
-// a 64-row tile, the reference's BQ * G = 64 mode, leaves the other 64 rows as zero padding).
+// Row-owner forward for 128-row query tiles (G heads x 128/G tokens sharing one selection row),
+// and 64-row tiles (the reference's BQ * G = 64 mode) on M = 64 MMAs (softmax_role_ro_m64).
 //
 // Same operation, selection semantics, unit order and loaders as nsa_sel_fwd_kernel (the
 // reference op's per-query-block mode, nsa_v2.cu:42-50, and the NSA window / compressed
@@ -51,6 +51,9 @@ struct CfgRO {
   static constexpr int kTmemCols = 512;
   static constexpr uint32_t kIdescS = ptx::idesc_bf16_f32(128, 128, false, false);
   static constexpr uint32_t kIdescPV = ptx::idesc_bf16_f32(128, DV, false, true);
+  // 64-row tiles (Params::ro_m64): M = 64, rows in TMEM lanes 0-15 of every 32-lane quarter
+  static constexpr uint32_t kIdescS64 = ptx::idesc_bf16_f32(64, 128, false, false);
+  static constexpr uint32_t kIdescPV64 = ptx::idesc_bf16_f32(64, DV, false, true);
 };
 
 template <class C>
@@ -86,6 +89,7 @@ __device__ void mma_s_role_ro(const Params& p, uint8_t* smem, SmemBars* bars, co
     uint32_t ui = 0, ne = 0, kc = 0;
     Ring k;
     const uint32_t k_base = ptx::smem_u32(smem + p.off_k), q_base = ptx::smem_u32(smem + p.off_q);
+    const uint32_t idesc = p.ro_m64 ? C::kIdescS64 : C::kIdescS;
     for (; ok; ++ui) {
       const int slot = ui % kInfoSlots;
       if (!w.wait(&bars->info_full[slot], (ui / kInfoSlots) & 1)) break;
@@ -112,7 +116,7 @@ __device__ void mma_s_role_ro(const Params& p, uint8_t* smem, SmemBars* bars, co
           for (int j = 0; j < C::DQK / 16; ++j) {
             const uint32_t ca = (j >> 2) * C::kQChunk + (j & 3) * 32;
             const uint32_t cb = (j >> 2) * C::kKChunkStride + (j & 3) * 32;
-            ptx::umma_bf16(dS, desc_add(aq0, ca), desc_add(bk0, cb), C::kIdescS, j > 0 ? 1u : 0u);
+            ptx::umma_bf16(dS, desc_add(aq0, ca), desc_add(bk0, cb), idesc, j > 0 ? 1u : 0u);
           }
           ptx::umma_commit(&bars->k_empty[k.idx]);
           ptx::umma_commit(&bars->s_full[sl]);
@@ -147,6 +151,7 @@ __device__ void mma_pv_role_ro(const Params& p, uint8_t* smem, SmemBars* bars, c
     uint32_t ui = 0, ne = 0, kc = 0;
     Ring v;
     const uint32_t v_base = ptx::smem_u32(smem + p.off_v);
+    const uint32_t idesc = p.ro_m64 ? C::kIdescPV64 : C::kIdescPV;
     for (; ok; ++ui) {
       const int slot = ui % kInfoSlots;
       if (!w.wait(&bars->info_full[slot], (ui / kInfoSlots) & 1)) break;
@@ -176,7 +181,7 @@ __device__ void mma_pv_role_ro(const Params& p, uint8_t* smem, SmemBars* bars, c
           for (int j = 0; j < 8; ++j) {
             if (j < nsc * 4) {
               const uint32_t cb = (j >> 2) * C::kVSub + (j & 3) * 2048;
-              ptx::umma_bf16_ts(dO, aP + (j >> 2) * 64 + (j & 3) * 8, desc_add(b0, cb), C::kIdescPV,
+              ptx::umma_bf16_ts(dO, aP + (j >> 2) * 64 + (j & 3) * 8, desc_add(b0, cb), idesc,
                                 (c == 0 && j == 0) ? 0u : 1u);
             }
           }
@@ -389,6 +394,192 @@ __device__ void softmax_role_ro(const Params& p, uint8_t* smem, SmemBars* bars, 
 }
 
 // ------------------------------------------------------------------------------------------
+// Softmax of a 64-row tile computed by M = 64 MMAs (Params::ro_m64).  Tile row 16q + j sits in
+// TMEM lane 32q + j (j < 16) of S, P and O.  The warp of quarter q in group h owns rows
+// 16q .. 16q + 15 through the 16-lane access shapes.  Thread t holds rows 16q + t/4 ("A") and
+// 16q + t/4 + 8 ("B"), at columns 8g + 2(t%4) and 8g + 2(t%4) + 1 of the group's 64 keys,
+// g = 0..7.  So each thread exps 32 scores per chunk, where the 128-row form of a 64-row tile
+// gives 64 to each thread of half the warps, and all eight softmax warps share the work.  The
+// four threads of a row combine their maxima and sums with two shuffles.
+// ------------------------------------------------------------------------------------------
+template <class C>
+__device__ void softmax_role_ro_m64(const Params& p, uint8_t* smem, SmemBars* bars, const Waiter& w,
+                                    uint32_t tmem, int h) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int i = threadIdx.x - (C::kSoftWarp + 4 * h) * 32;
+  const int quarter = warp & 3;
+  const int cp = lane & 3;                          // column pair inside every 8-column group
+  const int rA = quarter * 16 + (lane >> 2), rB = rA + 8;
+  const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+  float2* ml = reinterpret_cast<float2*>(smem + p.off_ml);
+  float* xmax = reinterpret_cast<float*>(smem + p.off_alpha);  // [chunk parity][half][row]
+  float* lsum1 = reinterpret_cast<float*>(smem + p.off_fac);   // [row]
+  const float sl2 = p.scale_log2;
+  const int ciA = rA % p.BQs, ciB = rB % p.BQs;
+  uint32_t ui = 0, ne = 0, kc = 0;
+  bool dead = false;
+
+  for (;; ++ui) {
+    const int slot = ui % kInfoSlots;
+    dead |= !w.wait_inline(&bars->info_full[slot], (ui / kInfoSlots) & 1);
+    if (ptx::named_bar_or(kWgBar0, 256, dead)) break;
+    const int* inf = info_slot(p, smem, slot);
+    if (inf[kInfStop]) break;
+    const int nsub = min(inf[kInfNsub], p.maxsub);
+    const int t0 = inf[kInfT0], kend = inf[kInfKend];
+    const int nch = (nsub + 1) >> 1;
+    if (nch == 0) {
+      if (h == 0 && i == 0) ptx::mbar_arrive(&bars->info_empty[slot]);
+      continue;
+    }
+    const int tA = t0 + ciA, tB = t0 + ciB;
+    int hiA = tA, loA = INT_MIN / 2, hiB = tB, loB = INT_MIN / 2, hi_all = t0, lo_all = INT_MIN / 2;
+    if constexpr (C::kExt) {
+      hiA = key_hi(p, tA);
+      loA = key_lo(p, tA);
+      hiB = key_hi(p, tB);
+      loB = key_lo(p, tB);
+      hi_all = key_hi(p, t0);
+      lo_all = key_lo(p, t0 + p.BQs - 1);
+    }
+    const uint32_t obase = tmem + lane_addr + C::kTmemO + (ne & 1) * C::DV;
+    float mA = -INFINITY, mB = -INFINITY, lA = 0.f, lB = 0.f;
+    bool first = true;
+
+    for (int c = 0; c < nch; ++c, ++kc) {
+      const int sl = (int)(kc & 1u);
+      dead |= !w.wait_inline(&bars->s_full[sl], (kc >> 1) & 1u);
+      ptx::tc_fence_after();
+      const uint32_t sbase = tmem + lane_addr + C::kTmemS + sl * 128 + 64 * h;
+      const int s0 = inf[kInfoHdr + 2 * c];
+      const bool has1 = (2 * c + 1) < nsub;
+      const int s1 = has1 ? inf[kInfoHdr + 2 * c + 1] : 0;
+      bool full = has1 && (max(s0, s1) + kSub - 1 <= hi_all) && (max(s0, s1) + kSub <= kend);
+      if constexpr (C::kExt) full = full && (min(s0, s1) >= lo_all);
+
+      float v[32];
+      ptx::tmem_ld16x256b_x8(sbase, v);
+      ptx::tmem_wait_ld();
+      if (!full) {
+#pragma unroll
+        for (int g = 0; g < 8; ++g)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int key = 64 * h + 8 * g + 2 * cp + e;
+            if (!ro_key_visible<C>(p, key, s0, s1, has1, hiA, loA, kend)) v[4 * g + e] = -INFINITY;
+            if (!ro_key_visible<C>(p, key, s0, s1, has1, hiB, loB, kend)) v[4 * g + 2 + e] = -INFINITY;
+          }
+      }
+      float xa = -INFINITY, xb = -INFINITY;
+#pragma unroll
+      for (int g = 0; g < 8; ++g) {
+        xa = fmaxf(xa, fmaxf(v[4 * g], v[4 * g + 1]));
+        xb = fmaxf(xb, fmaxf(v[4 * g + 2], v[4 * g + 3]));
+      }
+      xa = fmaxf(xa, __shfl_xor_sync(0xffffffffu, xa, 1));
+      xb = fmaxf(xb, __shfl_xor_sync(0xffffffffu, xb, 1));
+      xa = fmaxf(xa, __shfl_xor_sync(0xffffffffu, xa, 2));
+      xb = fmaxf(xb, __shfl_xor_sync(0xffffffffu, xb, 2));
+      float* xm = xmax + (kc & 1u) * 256;
+      if (cp == 0) {
+        xm[h * 128 + rA] = xa;
+        xm[h * 128 + rB] = xb;
+      }
+      ptx::named_bar_sync(kWgBar0, 256);
+      const float cA = fmaxf(xm[rA], xm[128 + rA]) * sl2, cB = fmaxf(xm[rB], xm[128 + rB]) * sl2;
+      float muA = mA, muB = mB, alA = 1.f, alB = 1.f;
+      bool need = false;
+      if (first) {
+        muA = cA;
+        muB = cB;
+      } else {
+        const float ca = fmaxf(mA, cA), cb = fmaxf(mB, cB);
+        if (ca > mA + kRescaleLog2) {
+          alA = (mA == -INFINITY) ? 0.f : ptx::ex2(mA - ca);
+          muA = ca;
+          need = true;
+        }
+        if (cb > mB + kRescaleLog2) {
+          alB = (mB == -INFINITY) ? 0.f : ptx::ex2(mB - cb);
+          muB = cb;
+          need = true;
+        }
+      }
+      // Group 0 rescales O (warp-uniform: the 16-lane accesses are .sync.aligned as well).
+      if (h == 0 && __any_sync(0xffffffffu, need)) {
+        dead |= !w.wait_inline(&bars->s_empty[(kc - 1) & 1u], ((kc - 1) >> 1) & 1u);
+        ptx::tc_fence_after();
+#pragma unroll
+        for (int h0 = 0; h0 < C::DV; h0 += 16) {
+          float o[8];
+          ptx::tmem_ld16x256b_x2(obase + h0, o);
+          ptx::tmem_wait_ld();
+#pragma unroll
+          for (int g = 0; g < 2; ++g) {
+            o[4 * g] *= alA;
+            o[4 * g + 1] *= alA;
+            o[4 * g + 2] *= alB;
+            o[4 * g + 3] *= alB;
+          }
+          ptx::tmem_st16x256b_x2(obase + h0, o);
+        }
+        ptx::tmem_wait_st();
+      }
+
+      // exp2, the partial row sums, and P as bf16 pairs: keys 8g + 2cp, 8g + 2cp + 1 of the
+      // group form pair 4g + cp, stored in column 64h + 4g + cp (the group's own score columns,
+      // already read).  mref is finite, so a masked score of -inf gives ex2(-inf) = 0.
+      const float mrA = (muA == -INFINITY) ? 0.f : muA, mrB = (muB == -INFINITY) ? 0.f : muB;
+      float sA = 0.f, sB = 0.f;
+      uint32_t pk[16];
+#pragma unroll
+      for (int g = 0; g < 8; ++g) {
+        const float a0 = ptx::ex2(fmaf(v[4 * g], sl2, -mrA)), a1 = ptx::ex2(fmaf(v[4 * g + 1], sl2, -mrA));
+        const float b0 = ptx::ex2(fmaf(v[4 * g + 2], sl2, -mrB)), b1 = ptx::ex2(fmaf(v[4 * g + 3], sl2, -mrB));
+        sA += a0 + a1;
+        sB += b0 + b1;
+        const __nv_bfloat162 ha = __floats2bfloat162_rn(a0, a1), hb = __floats2bfloat162_rn(b0, b1);
+        pk[2 * g] = *reinterpret_cast<const uint32_t*>(&ha);
+        pk[2 * g + 1] = *reinterpret_cast<const uint32_t*>(&hb);
+      }
+      ptx::tmem_st16x128b_x8(sbase, pk);
+      ptx::tmem_wait_st();
+      lA = lA * alA + sA;
+      lB = lB * alB + sB;
+      mA = muA;
+      mB = muB;
+      first = false;
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&bars->p_full[sl]);
+    }
+
+    // Row sums: the four threads of a row, then the two groups in group 0, which publishes
+    // (m, l) for the epilogue; the ml slot of unit ne was last read by the epilogue for unit ne - 2.
+    lA += __shfl_xor_sync(0xffffffffu, lA, 1);
+    lB += __shfl_xor_sync(0xffffffffu, lB, 1);
+    lA += __shfl_xor_sync(0xffffffffu, lA, 2);
+    lB += __shfl_xor_sync(0xffffffffu, lB, 2);
+    if (h == 1 && cp == 0) {
+      lsum1[rA] = lA;
+      lsum1[rB] = lB;
+    }
+    ptx::named_bar_sync(kWgBar0, 256);
+    if (h == 0) {
+      if (ne >= 2) dead |= !w.wait_inline(&bars->o_empty[ne & 1], ((ne >> 1) - 1) & 1);
+      if (cp == 0) {
+        ml[(ne & 1) * 128 + rA] = make_float2(mA, lA + lsum1[rA]);
+        ml[(ne & 1) * 128 + rB] = make_float2(mB, lB + lsum1[rB]);
+      }
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&bars->wg_done[ne & 1]);
+      if (i == 0) ptx::mbar_arrive(&bars->info_empty[slot]);
+    }
+    ++ne;
+  }
+}
+
+// ------------------------------------------------------------------------------------------
 // Epilogue: thread r scales O row r by w / l, writes the LSE, and stages the row into 128-byte
 // boxes (SW128 layout: 16-byte chunk j of row r at j ^ (r & 7)) that TMA stores, or adds with a
 // TMA reduce when the descriptor asks to accumulate.
@@ -400,12 +591,15 @@ __device__ void epilogue_role_ro(const CUtensorMap* tmO, const Params& p, uint8_
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int i = threadIdx.x - kEpiWarp0 * 32;
   const int quarter = warp & 3;
-  const int r = quarter * 32 + lane;
+  // The tile row held by this thread's TMEM lane; -1 for lanes 16-31 of a quarter, which the
+  // M = 64 layout leaves unused.
+  const int r = p.ro_m64 ? (lane < 16 ? quarter * 16 + lane : -1) : quarter * 32 + lane;
+  const int rr = r < 0 ? 0 : r;
   const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
   const float2* ml = reinterpret_cast<const float2*>(smem + p.off_ml);
   uint8_t* stg = smem + p.off_out;
   const float wgt = p.o_weight != nullptr ? __ldg(p.o_weight) : 1.f;
-  const int cg = r / p.BQs, ci = r - (r / p.BQs) * p.BQs;
+  const int cg = rr / p.BQs, ci = rr - (rr / p.BQs) * p.BQs;
   uint32_t ui = 0, ne = 0, nbox = 0;
   bool dead = false;
 
@@ -423,9 +617,9 @@ __device__ void epilogue_role_ro(const CUtensorMap* tmO, const Params& p, uint8_
       dead |= !w.wait(&bars->o_full[ne & 1], (ne >> 1) & 1);
       ptx::tc_fence_after();
     }
-    const float2 v_ml = nch > 0 ? ml[(ne & 1) * 128 + r] : make_float2(-INFINITY, 0.f);
+    const float2 v_ml = nch > 0 ? ml[(ne & 1) * 128 + rr] : make_float2(-INFINITY, 0.f);
     const float scale = v_ml.y > 0.f ? wgt / v_ml.y : 0.f;
-    if (r < p.G * p.BQs && ci < ntok && p.lse != nullptr) {
+    if (r >= 0 && r < p.G * p.BQs && ci < ntok && p.lse != nullptr) {
       const float lse = v_ml.y > 0.f ? (v_ml.x + log2f(v_ml.y)) * 0.69314718055994530942f : -INFINITY;
       p.lse[((size_t)b * p.Hq + (size_t)kvh * p.G + cg) * p.T + t0 + ci] = lse;
     }
@@ -446,9 +640,9 @@ __device__ void epilogue_role_ro(const CUtensorMap* tmO, const Params& p, uint8_
           }
         }
         if (nch > 0) ptx::tmem_wait_ld();
-        uint8_t* row = box + r * 128;
+        uint8_t* row = box + rr * 128;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
+        for (int j = 0; j < 8 && r >= 0; ++j) {
           uint4 q;
           if constexpr (sizeof(OutT) == 4) {
             q.x = __float_as_uint(v[4 * j + 0] * scale);
@@ -465,7 +659,7 @@ __device__ void epilogue_role_ro(const CUtensorMap* tmO, const Params& p, uint8_
             q.z = *reinterpret_cast<const uint32_t*>(&h2);
             q.w = *reinterpret_cast<const uint32_t*>(&h3);
           }
-          *reinterpret_cast<uint4*>(row + ((j ^ (r & 7)) << 4)) = q;
+          *reinterpret_cast<uint4*>(row + ((j ^ (rr & 7)) << 4)) = q;
         }
         ptx::fence_proxy_async_smem();
         ptx::named_bar_sync(kEpiBar, 128);
@@ -559,7 +753,10 @@ __global__ void __launch_bounds__(C::kThreads, 1)
   } else if (warp < C::kSoftWarp) {
     epilogue_role_ro<C>(&tmO, p, smem, bars, w, tmem);
   } else if (warp < C::kVLoadWarp) {
-    softmax_role_ro<C>(p, smem, bars, w, tmem, (warp - C::kSoftWarp) >> 2);
+    if (p.ro_m64)
+      softmax_role_ro_m64<C>(p, smem, bars, w, tmem, (warp - C::kSoftWarp) >> 2);
+    else
+      softmax_role_ro<C>(p, smem, bars, w, tmem, (warp - C::kSoftWarp) >> 2);
   } else if (warp == C::kVLoadWarp) {
     vloader_role<C>(&tmV, p, smem, bars, w, lane);
   } else if (warp == C::kPvWarp) {

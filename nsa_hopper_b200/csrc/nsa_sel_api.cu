@@ -485,6 +485,7 @@ int launch(const nsa_sel_desc* d, nsa_stream_t stream) {
   p.out_bufs = pl.out_bufs;
   p.o_accum = d->o_accumulate;
   p.o_weight = d->o_weight;
+  p.ro_m64 = (V.ro && pl.G * pl.BQs == 64 && !(d->debug_flags & NSA_DEBUG_RO_PAD128)) ? 1 : 0;
 
   {
     std::lock_guard<std::mutex> lk(g_dev.mu);

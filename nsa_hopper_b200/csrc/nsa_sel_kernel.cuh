@@ -121,6 +121,9 @@ struct Params {
   unsigned int* work_counter;
   int o_accum;             // 1: O += w * result through TMA reduce-add (fp32 O); 0: O = w * result
   const float* o_weight;   // device float w, or nullptr for 1
+  // Row-owner kernel, 64-row tiles: 1 = M = 64 MMAs (rows in TMEM lanes 0-15 of each 32-lane
+  // quarter, every softmax warp owns 16 rows); 0 = 128-row MMAs with 64 rows of zero padding.
+  int ro_m64;
 };
 
 // P tiles: NP buffers (4 for N <= 32 and d_qk <= 128, else 2), NP / NWG per softmax group; the k-th chunk of

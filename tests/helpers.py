@@ -29,7 +29,8 @@ def run_capi(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sel: torch.Tenso
              BQ: int = 1, cu_seqlens: Optional[torch.Tensor] = None, out_f32: bool = False,
              with_lse: bool = True, cyc: Optional[torch.Tensor] = None, err: Optional[torch.Tensor] = None,
              scale: float = 0.0, timeout_ms: int = 0, shard: Optional[Tuple[int, int, int, int]] = None,
-             o: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None, max_ctas: int = 0):
+             o: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None, max_ctas: int = 0,
+             debug_flags: int = 0):
     """Launch through nsa_sel_run on the current stream; returns (O, LSE) device tensors."""
     dev = torch.device("cuda")
     q, k, v = q.to(dev).contiguous(), k.to(dev).contiguous(), v.to(dev).contiguous()
@@ -48,7 +49,7 @@ def run_capi(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sel: torch.Tenso
         cyc=cyc.data_ptr() if cyc is not None else None, err=err.data_ptr() if err is not None else None,
         batch=B, heads_q=Hq, heads_kv=Hkv, seq_len=T, d_qk=dqk, d_v=dv, n_qblocks=sel.shape[2], n_sel=sel.shape[3],
         block_size=l_prime, q_block=BQ, o_dtype=capi.DTYPE_F32 if out_f32 else capi.DTYPE_BF16, scale=scale,
-        timeout_ms=timeout_ms, max_ctas=max_ctas)
+        timeout_ms=timeout_ms, max_ctas=max_ctas, debug_flags=debug_flags)
     if shard is not None:
         d.bkv_begin, d.bkv_end, d.qb_begin, d.qb_end = shard
     capi.run(d, torch.cuda.current_stream().cuda_stream)
