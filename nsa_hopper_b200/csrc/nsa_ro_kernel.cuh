@@ -212,15 +212,15 @@ __device__ void mma_pv_role_ro(const Params& p, uint8_t* smem, SmemBars* bars, c
 // ------------------------------------------------------------------------------------------
 // Softmax: thread r owns query row r (TMEM lane r) of every chunk.
 // ------------------------------------------------------------------------------------------
-template <class C>
-__device__ __forceinline__ bool ro_key_visible(const Params& p, int key, int s0, int s1, bool has1, int hi,
-                                               int lo, int kend) {
-  const int sb = key >> 6;
-  const int kpos = (sb ? s1 : s0) + (key & 63);
-  if constexpr (C::kExt)
-    return (sb == 0 || has1) && kpos <= hi && kpos >= lo && kpos < kend;
-  else
-    return (sb == 0 || has1) && kpos <= hi && kpos < kend;
+// Key visibility inside one 64-key sub-block that starts at key position s: the key at offset j
+// is visible to a row iff the sub-block exists and lo <= s + j <= hi, s + j < kend (lo is
+// INT_MIN / 2 without a window).  Those offsets form one interval [a, a + w) (w = 0: none), so
+// masking an element is the single unsigned compare (j - a) < w.
+__device__ __forceinline__ void ro_sub_interval(int s, bool exists, int hi, int lo, int kend, int& a, unsigned& w) {
+  const int a0 = max(lo - s, 0);
+  const int b0 = min(min(hi + 1, kend) - s, kSub);
+  a = a0;
+  w = (exists && b0 > a0) ? (unsigned)(b0 - a0) : 0u;
 }
 
 template <class C>
@@ -282,11 +282,15 @@ __device__ void softmax_role_ro(const Params& p, uint8_t* smem, SmemBars* bars, 
       dead |= !w.wait_inline(&bars->s_full[sl], (kc >> 1) & 1u);
       ptx::tc_fence_after();
       const uint32_t sbase = tmem + lane_addr + C::kTmemS + sl * 128 + 64 * h;
-      const int s0 = inf[kInfoHdr + 2 * c];
-      const bool has1 = (2 * c + 1) < nsub;
-      const int s1 = has1 ? inf[kInfoHdr + 2 * c + 1] : 0;
-      bool full = has1 && (max(s0, s1) + kSub - 1 <= hi_all) && (max(s0, s1) + kSub <= kend);
-      if constexpr (C::kExt) full = full && (min(s0, s1) >= lo_all);
+      // This group's keys are exactly sub-block h of the chunk.  It needs a mask only when some
+      // row does not see all of that sub-block; each row's visible part is one interval.
+      const bool has = h == 0 || (2 * c + 1) < nsub;
+      const int sh = has ? inf[kInfoHdr + 2 * c + h] : 0;
+      bool full = has && (sh + kSub - 1 <= hi_all) && (sh + kSub <= kend);
+      if constexpr (C::kExt) full = full && (sh >= lo_all);
+      int ma = 0;
+      unsigned mw = kSub;
+      if (!full) ro_sub_interval(sh, has, hi, lo, kend, ma, mw);
 
       // pass 1: the row's max over this group's 64 keys, combined with the other group's
       float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
@@ -298,7 +302,7 @@ __device__ void softmax_role_ro(const Params& p, uint8_t* smem, SmemBars* bars, 
         if (!full) {
 #pragma unroll
           for (int j = 0; j < 32; ++j)
-            if (!ro_key_visible<C>(p, 64 * h + 32 * b + j, s0, s1, has1, hi, lo, kend)) v[j] = -INFINITY;
+            if ((unsigned)(32 * b + j - ma) >= mw) v[j] = -INFINITY;
         }
 #pragma unroll
         for (int j = 0; j < 32; ++j) mx[j & 3] = fmaxf(mx[j & 3], v[j]);
@@ -354,7 +358,7 @@ __device__ void softmax_role_ro(const Params& p, uint8_t* smem, SmemBars* bars, 
         if (!full) {
 #pragma unroll
           for (int j = 0; j < 32; ++j)
-            if (!ro_key_visible<C>(p, 64 * h + 32 * b + j, s0, s1, has1, hi, lo, kend)) v[j] = -INFINITY;
+            if ((unsigned)(32 * b + j - ma) >= mw) v[j] = -INFINITY;
         }
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = ptx::ex2(fmaf(v[j], sl2, -mref));
@@ -451,23 +455,27 @@ __device__ void softmax_role_ro_m64(const Params& p, uint8_t* smem, SmemBars* ba
       dead |= !w.wait_inline(&bars->s_full[sl], (kc >> 1) & 1u);
       ptx::tc_fence_after();
       const uint32_t sbase = tmem + lane_addr + C::kTmemS + sl * 128 + 64 * h;
-      const int s0 = inf[kInfoHdr + 2 * c];
-      const bool has1 = (2 * c + 1) < nsub;
-      const int s1 = has1 ? inf[kInfoHdr + 2 * c + 1] : 0;
-      bool full = has1 && (max(s0, s1) + kSub - 1 <= hi_all) && (max(s0, s1) + kSub <= kend);
-      if constexpr (C::kExt) full = full && (min(s0, s1) >= lo_all);
+      // as in the 128-row form: this group's keys are sub-block h, masked by one interval per row
+      const bool has = h == 0 || (2 * c + 1) < nsub;
+      const int sh = has ? inf[kInfoHdr + 2 * c + h] : 0;
+      bool full = has && (sh + kSub - 1 <= hi_all) && (sh + kSub <= kend);
+      if constexpr (C::kExt) full = full && (sh >= lo_all);
 
       float v[32];
       ptx::tmem_ld16x256b_x8(sbase, v);
       ptx::tmem_wait_ld();
       if (!full) {
+        int aA, aB;
+        unsigned wA, wB;
+        ro_sub_interval(sh, has, hiA, loA, kend, aA, wA);
+        ro_sub_interval(sh, has, hiB, loB, kend, aB, wB);
+        const int oA = 2 * cp - aA, oB = 2 * cp - aB;  // element (g, e) sits at offset 8g + 2cp + e
 #pragma unroll
         for (int g = 0; g < 8; ++g)
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            const int key = 64 * h + 8 * g + 2 * cp + e;
-            if (!ro_key_visible<C>(p, key, s0, s1, has1, hiA, loA, kend)) v[4 * g + e] = -INFINITY;
-            if (!ro_key_visible<C>(p, key, s0, s1, has1, hiB, loB, kend)) v[4 * g + 2 + e] = -INFINITY;
+            if ((unsigned)(8 * g + e + oA) >= wA) v[4 * g + e] = -INFINITY;
+            if ((unsigned)(8 * g + e + oB) >= wB) v[4 * g + 2 + e] = -INFINITY;
           }
       }
       float xa = -INFINITY, xb = -INFINITY;
