@@ -290,8 +290,8 @@ int make_plan(const nsa_sel_desc* d, int sm_count, Plan* pl) {
   const int of32 = d->o_dtype == NSA_DTYPE_F32 ? 1 : 0;
   int bqs = 1, ncol = 16, vi = -1;
   if (!(d->debug_flags & NSA_DEBUG_NO_ROW_OWNER)) {
-    // 128 query rows per tile, or 64 (the reference's BQ * G = 64 mode) with the tile's other
-    // rows left as zero padding
+    // 128 query rows per tile, or 64 (the reference's BQ * G = 64 mode, on M = 64 MMAs unless
+    // NSA_DEBUG_RO_PAD128 asks for the padded 128-row form)
     for (int rows = 128; rows >= 64 && vi < 0; rows -= 64) {
       if (rows % G != 0 || d->q_block % (rows / G) != 0) continue;
       vi = find_variant(d->d_qk, d->d_v, 128, of32, ext);

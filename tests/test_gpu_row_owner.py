@@ -1,6 +1,7 @@
 """The row-owner kernel (nsa_ro_kernel.cuh: query rows on the MMA's M, P in tensor memory)
-against the oracle, on the shapes that route to it: tiles of 128 query rows, or 64 with the rest
-zero padding (G divides the tile's rows and BQ is a multiple of rows / G)."""
+against the oracle, on the shapes that route to it: tiles of 128 query rows, or 64 (G divides the
+tile's rows and BQ is a multiple of rows / G; 64-row tiles run on M = 64 MMAs, covered further by
+tests/test_gpu_ro_m64.py)."""
 import numpy as np
 import pytest
 import torch
