@@ -861,6 +861,112 @@ def run_select(args):
     }
 
 
+def run_backward(args):
+    """--stage backward: the selected branch's backward (nsa_sel_backward: row sums dO.O, the
+    inverse selection index and the tcgen05 gradient kernel), with the fp32 gradient buffers
+    zeroed inside the timed step, on the workload's shapes (d = 128, G = 8 or 16).  Algorithmic
+    FLOPs: five products of 2*d per (query row, visible key) -- S and dP recomputed, dV, dK, dQ
+    -- i.e. 2.5x the forward's, against the measured bf16 tensor peak.  After timing, dQ of a
+    128-token window per KV head is compared with the CPU restatement (oracle/backward.py) and the
+    exact sum identities (dV summed over keys = dO summed over rows; dK summed over keys = 0) are
+    checked on the whole output."""
+    import torch
+
+    import oracle.backward as obwd
+    from nsa_hopper_b200 import capi, workload
+
+    w = workload.CONFIGS[args.config]
+    if w.n_seqs or w.d_qk != 128 or w.d_v != 128 or w.G not in (8, 16):
+        raise SystemExit(f"--stage backward: workload {args.config} is outside the backward kernel "
+                         "(d = 128, G = 8 or 16, no varlen)")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    B, T, Hq, Hkv, D, lp, n = w.B, w.T, w.Hq, w.Hkv, w.d_qk, w.block, w.n
+    sel_np = workload.make_indices(w, args.seed)
+    gen = torch.Generator(device=dev).manual_seed(args.seed)
+    q = torch.randn(B, Hq, T, D, device=dev, generator=gen).to(torch.bfloat16)
+    k = torch.randn(B, Hkv, T, D, device=dev, generator=gen).to(torch.bfloat16)
+    v = torch.randn(B, Hkv, T, D, device=dev, generator=gen).to(torch.bfloat16)
+    d_o = torch.randn(B, Hq, T, D, device=dev, generator=gen).to(torch.bfloat16)
+    sel = torch.from_numpy(sel_np).to(dev)
+    o = torch.empty(B, Hq, T, D, device=dev, dtype=torch.bfloat16)
+    lse = torch.empty(B, Hq, T, device=dev, dtype=torch.float32)
+    err = torch.zeros(1, device=dev, dtype=torch.int32)
+    stream = torch.cuda.current_stream(dev)
+    fwd = capi.make_desc(q=q.data_ptr(), k=k.data_ptr(), v=v.data_ptr(), sel=sel.data_ptr(), o=o.data_ptr(),
+                         lse=lse.data_ptr(), err=err.data_ptr(), batch=B, heads_q=Hq, heads_kv=Hkv, seq_len=T,
+                         d_qk=D, d_v=D, n_qblocks=T, n_sel=n, block_size=lp, q_block=1, o_dtype=capi.DTYPE_BF16)
+    capi.run(fwd, stream.cuda_stream)
+    dq = torch.empty(B, Hq, T, D, device=dev, dtype=torch.float32)
+    dk = torch.empty(B, Hkv, T, D, device=dev, dtype=torch.float32)
+    dv = torch.empty_like(dk)
+    desc = capi.make_bwd_desc(q=q.data_ptr(), k=k.data_ptr(), v=v.data_ptr(), sel=sel.data_ptr(), o=o.data_ptr(),
+                              lse=lse.data_ptr(), d_o=d_o.data_ptr(), dq=dq.data_ptr(), dk=dk.data_ptr(),
+                              dv=dv.data_ptr(), err=err.data_ptr(), batch=B, heads_q=Hq, heads_kv=Hkv, seq_len=T,
+                              d=D, n_sel=n, block_size=lp, o_dtype=capi.DTYPE_BF16)
+    ws = torch.empty(capi.backward_workspace_bytes(desc), device=dev, dtype=torch.uint8)
+    desc.workspace = ws.data_ptr()
+    flush = torch.empty(FLUSH_BYTES // 4, device=dev, dtype=torch.float32)
+
+    def step():
+        dq.zero_()
+        dk.zero_()
+        dv.zero_()
+        capi.backward(desc, stream.cuda_stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if int(err.item()) != 0:
+        raise RuntimeError(f"backward kernel reported device error {int(err.item())}")
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    with ClockSampler(0) as clk:
+        for i in range(args.steps):
+            flush.fill_(float(i))
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+        torch.cuda.synchronize()
+    ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
+    if int(err.item()) != 0:
+        raise RuntimeError(f"backward kernel reported device error {int(err.item())}")
+    work = workload.algorithmic_work(w, sel_np)
+    flops = 2.5 * work["flops"]
+    pk = measured_peaks()
+    achieved = flops / (ms * 1e-3) / 1e12
+    # parity: dQ windows against the restatement, sum identities on everything
+    G = Hq // Hkv
+    qc, kc, vc, doc = q.cpu(), k.cpu(), v.cpu(), d_o.cpu()
+    worst = 0.0
+    for kvh in range(min(Hkv, 4)):
+        h, t0 = kvh * G + (kvh * 5) % G, max(0, T - 128 - 997 * kvh)
+        r = obwd.dq_rows(qc, kc, vc, sel_np, lp, doc, 0, h, t0, t0 + 128)
+        x = dq[0, h, t0:t0 + 128].double().cpu().numpy()
+        worst = max(worst, float(np.abs(x - r).max() / max(np.abs(r).max(), 1e-30)))
+    sum_do = d_o.double().view(B, Hkv, G, T, D).sum((2, 3))
+    dv_gap = float(((dv.double().sum(2) - sum_do).abs() / d_o.double().abs().view(B, Hkv, G, T, D).sum((2, 3))).max())
+    dk_gap = float((dk.double().sum(2).abs() / dk.double().abs().sum(2).clamp_min(1e-30)).max())
+    return {
+        "metric": "selected-branch backward tokens/s", "value": B * T / (ms * 1e-3), "unit": "tokens/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16 in, bf16 P/dS, fp32 accumulate and gradients",
+        "data": "synthetic N(0,1) bf16 Q/K/V/dO, seeded BASELINE index rule",
+        "config": {"workload": args.config, "stage": "backward", "B": B, "T": T, "Hq": Hq, "Hkv": Hkv, "d": D,
+                   "block": lp, "top_n": n, "l2": "256 MiB buffer written between timed steps (L2 flushed)",
+                   "timed": "zeroing dQ/dK/dV + nsa_sel_backward (row sums, index, gradient kernel)"},
+        "tflops": achieved,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": achieved / pk["bf16_tflops"], "traffic": None,
+                     "peak_kind": f"{pk['kind']} (MEASURED_PEAKS.json bf16_tflops, burst)",
+                     "algorithmic_flops_per_launch": flops},
+        "parity": {"dq_window_scaled_err": worst, "dv_sum_identity_rel": dv_gap, "dk_sum_identity_rel": dk_gap,
+                   "tol_scaled": 2e-2, "ok": worst <= 2e-2,
+                   "sample": "dQ of a 128-token window of one head per KV head vs oracle/backward.py (fp64)"},
+        "e2e": None, "clocks": clk.summary(), "gpu_launches": 6 * args.steps, "cpu_baseline": None,
+    }
+
+
 def run_nsa(args):
     """--stage nsa: the full NSA forward (nsa_hopper_b200.nsa.nsa_forward: compression, the block
     selection kernel, the selected / sliding-window / compressed branches on the attention kernel
@@ -935,10 +1041,11 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gather", action="store_true", help="skip the separately timed all-gather (N > 1)")
-    ap.add_argument("--stage", choices=["selected", "select", "nsa", "refsweep", "peaks"], default="selected",
+    ap.add_argument("--stage", choices=["selected", "select", "nsa", "refsweep", "peaks", "backward"],
+                    default="selected",
                     help="selected: the selected-branch forward (the headline); select: the block-selection kernel; "
                          "nsa: the full NSA forward; refsweep: the reference's published sweep rows; peaks: the "
-                         "on-chip ceiling microbenchmarks")
+                         "on-chip ceiling microbenchmarks; backward: the selected branch's backward")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -948,7 +1055,8 @@ def main():
 
     if args.stage != "selected":
         if rank == 0:
-            fn = {"select": run_select, "nsa": run_nsa, "refsweep": run_refsweep, "peaks": run_peaks}[args.stage]
+            fn = {"select": run_select, "nsa": run_nsa, "refsweep": run_refsweep, "peaks": run_peaks,
+                  "backward": run_backward}[args.stage]
             print(json.dumps(fn(args)), flush=True)
         return
 

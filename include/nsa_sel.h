@@ -212,6 +212,48 @@ int nsa_sel_select_noalloc(const void* q, const void* k, int32_t* sel_out, int32
                            int32_t T, int32_t d, int32_t l_prime, int32_t n_sel, int32_t cmp_block,
                            int32_t cmp_stride, nsa_stream_t stream);
 
+/* Backward of the selected-branch forward.  The reference has no backward pass (its README
+   (2).md:85 lists it as missing); these entry points give the gradients of the same attention
+   (ref_only.py:2-20, nsa_reference.py:18-25) with respect to Q, K and V:
+       P = exp(scale * q.k - LSE),  dP = dO . v,  dS = P * (dP - sum_d dO * O),
+       dQ = scale * dS K,  dK = scale * dS^T Q,  dV = P^T dO
+   over the keys each query token sees in the forward (per-token selection, BQ == 1; same
+   duplicate, padding and causal rules).  Supported: d_qk == d_v == 128, G = Hq / Hkv in {8, 16},
+   l_prime in {64, 128, 256}, no cu_seqlens.  Zero-initialise, then fill the fields. */
+typedef struct nsa_sel_bwd_desc {
+  const void* q;              /* bf16 [B, Hq, T, 128] */
+  const void* k;              /* bf16 [B, Hkv, T, 128] */
+  const void* v;              /* bf16 [B, Hkv, T, 128] */
+  const int32_t* sel;         /* int32 [B, Hkv, T, KSEL] */
+  const void* o;              /* the forward's O [B, Hq, T, 128], dtype o_dtype */
+  const float* lse;           /* the forward's LSE, fp32 [B, Hq, T] */
+  const void* d_o;            /* bf16 [B, Hq, T, 128]: gradient of the loss with respect to O */
+  float* dq;                  /* fp32 [B, Hq, T, 128]  } accumulated into (atomic adds): */
+  float* dk;                  /* fp32 [B, Hkv, T, 128] } zero them first for plain gradients */
+  float* dv;                  /* fp32 [B, Hkv, T, 128] } */
+  void* workspace;            /* nsa_sel_backward_workspace_bytes() bytes, 16-byte aligned */
+  int32_t* err;               /* optional device int32; NSA_DEVERR_* bits are ORed into it */
+  int32_t batch, heads_q, heads_kv, seq_len, d;
+  int32_t n_sel;              /* KSEL */
+  int32_t block_size;         /* l_prime: 64, 128 or 256 */
+  int32_t o_dtype;            /* NSA_DTYPE_BF16 or NSA_DTYPE_F32 */
+  float scale;                /* softmax scale of the forward; <= 0 selects 1/sqrt(d) */
+  int32_t timeout_ms;         /* bound on every in-kernel wait; 0 = default (2000 ms) */
+  int32_t max_ctas;           /* 0 = one CTA per SM */
+  int32_t reserved[5];
+} nsa_sel_bwd_desc;
+
+/* Bytes of the workspace nsa_sel_backward needs for a description (the row sums dO . O and the
+   inverse selection index: about 4 * (B*Hq*T + 2 * B*Hkv*T*KSEL*l_prime/64) bytes), or -1 if
+   the description is invalid (see nsa_sel_last_error()). */
+int64_t nsa_sel_backward_workspace_bytes(const nsa_sel_bwd_desc* desc);
+
+/* Adds dQ, dK, dV for the description on `stream` (six kernel launches and one memset, no
+   allocation, asynchronous): the row sums dO . O, the inverse index (per (b, kvh, 64-key
+   sub-block) the tokens that attend to it) and the tcgen05 gradient kernel.  The sums are
+   accumulated with atomic adds, so the last bits may differ between runs. */
+int nsa_sel_backward(const nsa_sel_bwd_desc* desc, nsa_stream_t stream);
+
 /* Size in bytes of the static scratch used by nsa_sel_select_noalloc. */
 int64_t nsa_sel_select_static_scratch_bytes(void);
 

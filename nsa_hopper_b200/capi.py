@@ -79,6 +79,21 @@ class NsaSelHostIO(ctypes.Structure):
     ]
 
 
+class NsaSelBwdDesc(ctypes.Structure):
+    """Mirror of ``nsa_sel_bwd_desc``."""
+
+    _fields_ = [
+        ("q", ctypes.c_void_p), ("k", ctypes.c_void_p), ("v", ctypes.c_void_p), ("sel", ctypes.c_void_p),
+        ("o", ctypes.c_void_p), ("lse", ctypes.c_void_p), ("d_o", ctypes.c_void_p),
+        ("dq", ctypes.c_void_p), ("dk", ctypes.c_void_p), ("dv", ctypes.c_void_p),
+        ("workspace", ctypes.c_void_p), ("err", ctypes.c_void_p),
+        ("batch", ctypes.c_int32), ("heads_q", ctypes.c_int32), ("heads_kv", ctypes.c_int32),
+        ("seq_len", ctypes.c_int32), ("d", ctypes.c_int32), ("n_sel", ctypes.c_int32),
+        ("block_size", ctypes.c_int32), ("o_dtype", ctypes.c_int32), ("scale", ctypes.c_float),
+        ("timeout_ms", ctypes.c_int32), ("max_ctas", ctypes.c_int32), ("reserved", ctypes.c_int32 * 5),
+    ]
+
+
 class NsaSelError(RuntimeError):
     def __init__(self, code: int, message: str):
         super().__init__(f"nsa_sel error {code}: {message}")
@@ -121,6 +136,10 @@ def load(path: Optional[str] = None) -> ctypes.CDLL:
     lib.nsa_sel_select_noalloc.restype = ctypes.c_int
     lib.nsa_sel_select_static_scratch_bytes.argtypes = []
     lib.nsa_sel_select_static_scratch_bytes.restype = ctypes.c_int64
+    lib.nsa_sel_backward_workspace_bytes.argtypes = [ctypes.POINTER(NsaSelBwdDesc)]
+    lib.nsa_sel_backward_workspace_bytes.restype = ctypes.c_int64
+    lib.nsa_sel_backward.argtypes = [ctypes.POINTER(NsaSelBwdDesc), vp]
+    lib.nsa_sel_backward.restype = ctypes.c_int
     lib.nsa_sel_select_status.argtypes = []
     lib.nsa_sel_select_status.restype = ctypes.c_int32
     if path is None:
@@ -201,3 +220,26 @@ def make_host_io(**kw) -> NsaSelHostIO:
 def run_host(desc: NsaSelDesc, io: NsaSelHostIO, stream: int = 0) -> None:
     """nsa_sel_run_host: host inputs in, host outputs back, copies pipelined with the kernel."""
     check(load().nsa_sel_run_host(ctypes.byref(desc), ctypes.byref(io), ctypes.c_void_p(stream)))
+
+
+def make_bwd_desc(**kw) -> NsaSelBwdDesc:
+    d = NsaSelBwdDesc()
+    ctypes.memset(ctypes.addressof(d), 0, ctypes.sizeof(d))
+    for key, val in kw.items():
+        if not hasattr(d, key):
+            raise KeyError(key)
+        setattr(d, key, val)
+    return d
+
+
+def backward_workspace_bytes(desc: NsaSelBwdDesc) -> int:
+    """nsa_sel_backward_workspace_bytes (raises on an invalid description)."""
+    n = int(load().nsa_sel_backward_workspace_bytes(ctypes.byref(desc)))
+    if n < 0:
+        raise NsaSelError(NSA_ERR_INVALID_ARG, last_error())
+    return n
+
+
+def backward(desc: NsaSelBwdDesc, stream: int = 0) -> None:
+    """nsa_sel_backward: adds dQ, dK, dV of the selected branch (see include/nsa_sel.h)."""
+    check(load().nsa_sel_backward(ctypes.byref(desc), ctypes.c_void_p(stream)))

@@ -11,6 +11,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 #include <math.h>
+#include <algorithm>
 #include <mutex>
 #include <stdarg.h>
 #include <stdio.h>
@@ -22,6 +23,7 @@
 #include "nsa_ro_kernel.cuh"
 #include "nsa_select_kernel.cuh"
 #include "nsa_select_tc_kernel.cuh"
+#include "nsa_bwd_kernel.cuh"
 
 namespace {
 
@@ -772,9 +774,185 @@ int run_host(const nsa_sel_desc* d, const nsa_sel_host_io* io, nsa_stream_t stre
   return NSA_OK;
 }
 
+// ------------------------------------------------------------------ backward
+struct BwdLayout {
+  size_t off_delta, off_counts, off_fill, off_tok_off, off_item_off, off_tokens, off_items, total;
+  int n_buckets, nsub, spb, n_blk, G;
+  long long max_pairs;
+};
+
+size_t align16(size_t x) { return (x + 15) / 16 * 16; }
+
+int bwd_layout(const nsa_sel_bwd_desc* d, BwdLayout* L) {
+  if (d == nullptr) return fail(NSA_ERR_INVALID_ARG, "desc is NULL");
+  const int B = d->batch, Hq = d->heads_q, Hkv = d->heads_kv, T = d->seq_len;
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || T <= 0) return fail(NSA_ERR_INVALID_ARG, "B, Hq, Hkv, T must be positive");
+  if (Hq % Hkv != 0) return fail(NSA_ERR_INVALID_ARG, "Hq (%d) must be a multiple of Hkv (%d)", Hq, Hkv);
+  const int G = Hq / Hkv;
+  if (G != 8 && G != 16) return fail(NSA_ERR_UNSUPPORTED, "backward: group size G=%d; built for G = 8 and 16", G);
+  if (d->d != nsa::bwd::kD) return fail(NSA_ERR_UNSUPPORTED, "backward: d=%d; built for d = 128", d->d);
+  if (d->block_size != 64 && d->block_size != 128 && d->block_size != 256)
+    return fail(NSA_ERR_UNSUPPORTED, "l_prime=%d: the kernel family supports 64, 128 and 256", d->block_size);
+  if (d->n_sel <= 0 || d->n_sel > 64) return fail(NSA_ERR_INVALID_ARG, "KSEL must be in 1..64");
+  if (d->o_dtype != NSA_DTYPE_BF16 && d->o_dtype != NSA_DTYPE_F32)
+    return fail(NSA_ERR_INVALID_ARG, "o_dtype must be NSA_DTYPE_BF16 or NSA_DTYPE_F32");
+  if ((long long)T >= (1ll << 24) || (long long)B * Hq * T >= (1ll << 31))
+    return fail(NSA_ERR_UNSUPPORTED, "problem too large for 32-bit token indices");
+  L->G = G;
+  L->spb = d->block_size / 64;
+  L->n_blk = (T + d->block_size - 1) / d->block_size;
+  L->nsub = (T + 63) / 64;
+  const long long n_bkv = (long long)B * Hkv;
+  L->n_buckets = (int)(n_bkv * L->nsub);
+  if (n_bkv * L->nsub >= (1ll << 30)) return fail(NSA_ERR_UNSUPPORTED, "too many (b, kvh, sub-block) buckets");
+  const long long per_row = std::min<long long>((long long)d->n_sel * L->spb, L->nsub);
+  L->max_pairs = n_bkv * T * per_row;
+  if (L->max_pairs >= (1ll << 31)) return fail(NSA_ERR_UNSUPPORTED, "selection index exceeds 2^31 entries");
+  const long long max_items = L->max_pairs / nsa::bwd::kItemTokens + L->n_buckets;
+  size_t o = 0;
+  L->off_delta = o; o = align16(o + (size_t)B * Hq * T * 4);
+  L->off_counts = o; o = align16(o + (size_t)L->n_buckets * 4);
+  L->off_fill = o; o = align16(o + (size_t)L->n_buckets * 4);
+  L->off_tok_off = o; o = align16(o + (size_t)L->n_buckets * 4);
+  L->off_item_off = o; o = align16(o + (size_t)(L->n_buckets + 1) * 4);
+  L->off_tokens = o; o = align16(o + (size_t)L->max_pairs * 4);
+  L->off_items = o; o = align16(o + (size_t)max_items * 16);
+  L->total = o;
+  return NSA_OK;
+}
+
+bool g_bwd_attr[kMaxDevices] = {};
+
+int backward(const nsa_sel_bwd_desc* d, nsa_stream_t stream) {
+  BwdLayout L;
+  int rc = bwd_layout(d, &L);
+  if (rc != NSA_OK) return rc;
+  if (d->q == nullptr || d->k == nullptr || d->v == nullptr || d->sel == nullptr || d->o == nullptr ||
+      d->lse == nullptr || d->d_o == nullptr || d->dq == nullptr || d->dk == nullptr || d->dv == nullptr ||
+      d->workspace == nullptr)
+    return fail(NSA_ERR_INVALID_ARG, "q, k, v, sel, o, lse, d_o, dq, dk, dv and workspace must be non-NULL");
+  if (!aligned16(d->q) || !aligned16(d->k) || !aligned16(d->v) || !aligned16(d->o) || !aligned16(d->d_o) ||
+      !aligned16(d->dq) || !aligned16(d->dk) || !aligned16(d->dv) || !aligned16(d->workspace))
+    return fail(NSA_ERR_INVALID_ARG, "q, k, v, o, d_o, dq, dk, dv and workspace must be 16-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(d->sel) & 3u) != 0 || (reinterpret_cast<uintptr_t>(d->lse) & 3u) != 0)
+    return fail(NSA_ERR_INVALID_ARG, "sel and lse must be 4-byte aligned");
+  int sm = 0, dev = 0;
+  rc = current_sm_count(&sm, &dev);
+  if (rc != NSA_OK) return rc;
+  const int B = d->batch, Hq = d->heads_q, Hkv = d->heads_kv, T = d->seq_len, G = L.G;
+  const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(d->workspace);
+  float* delta = reinterpret_cast<float*>(ws + L.off_delta);
+  int* counts = reinterpret_cast<int*>(ws + L.off_counts);
+  int* fillc = reinterpret_cast<int*>(ws + L.off_fill);
+  int* tok_off = reinterpret_cast<int*>(ws + L.off_tok_off);
+  int* item_off = reinterpret_cast<int*>(ws + L.off_item_off);
+  int32_t* tokens = reinterpret_cast<int32_t*>(ws + L.off_tokens);
+  int4* items = reinterpret_cast<int4*>(ws + L.off_items);
+
+  // tensor maps: Q and dO per token (G heads x 64 dims per box), K and V per 64-key sub-block
+  CUtensorMap tmQ, tmDO, tmK, tmV;
+  {
+    const cuuint64_t dims[4] = {128, (cuuint64_t)T, (cuuint64_t)Hq, (cuuint64_t)B};
+    const cuuint64_t str[3] = {256, 256ull * T, 256ull * T * Hq};
+    const cuuint32_t box[4] = {64, 1, (cuuint32_t)G, 1};
+    rc = encode(&tmQ, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, d->q, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "Q");
+    if (rc == NSA_OK)
+      rc = encode(&tmDO, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, d->d_o, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "dO");
+    if (rc != NSA_OK) return rc;
+  }
+  {
+    const cuuint64_t dims[4] = {64, (cuuint64_t)T, 2, (cuuint64_t)B * Hkv};
+    const cuuint64_t str[3] = {256, 128, 256ull * T};
+    const cuuint32_t box[4] = {64, 64, 2, 1};
+    rc = encode(&tmK, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, d->k, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "K");
+    if (rc == NSA_OK)
+      rc = encode(&tmV, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, d->v, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "V");
+    if (rc != NSA_OK) return rc;
+  }
+  {
+    std::lock_guard<std::mutex> lk(g_dev.mu);
+    if (!g_bwd_attr[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(&nsa::bwd::nsa_bwd_kernel),
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)nsa::bwd::kSmemBytes);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(backward smem)");
+      g_bwd_attr[dev] = true;
+    }
+  }
+
+  // 1. row sums dO . O
+  const long long rows = (long long)B * Hq * T;
+  if (d->o_dtype == NSA_DTYPE_BF16)
+    nsa::bwd::delta_kernel<__nv_bfloat16><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(d->d_o), static_cast<const __nv_bfloat16*>(d->o), delta, rows);
+  else
+    nsa::bwd::delta_kernel<float><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(d->d_o), static_cast<const float*>(d->o), delta, rows);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "backward row-sum kernel launch");
+  // 2. inverse index: counts, offsets, token lists, work items
+  e = cudaMemsetAsync(counts, 0, L.off_tok_off - L.off_counts, st);  // counts and fill counters
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(backward index counters)");
+  nsa::bwd::IndexShape sh{B * Hkv, T, d->n_sel, L.spb, L.n_blk, L.nsub, nsa::bwd::kItemTokens};
+  const unsigned row_blocks = (unsigned)(((long long)B * Hkv * T + 255) / 256);
+  nsa::bwd::index_rows_kernel<false><<<row_blocks, 256, 0, st>>>(d->sel, sh, counts, nullptr, nullptr, nullptr);
+  nsa::bwd::index_scan_kernel<<<1, 1024, 0, st>>>(counts, L.n_buckets, nsa::bwd::kItemTokens, tok_off, item_off);
+  nsa::bwd::index_rows_kernel<true><<<row_blocks, 256, 0, st>>>(d->sel, sh, nullptr, tok_off, fillc, tokens);
+  nsa::bwd::index_items_kernel<<<(unsigned)((L.n_buckets + 255) / 256), 256, 0, st>>>(sh, counts, tok_off, item_off,
+                                                                                      items);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "backward index kernel launch");
+  // 3. gradients
+  nsa::bwd::Params p{};
+  p.tokens = tokens;
+  p.items = reinterpret_cast<const int32_t*>(items);
+  p.lse = d->lse;
+  p.delta = delta;
+  p.dq = d->dq;
+  p.dk = d->dk;
+  p.dv = d->dv;
+  p.err = d->err;
+  p.n_items_ptr = item_off + L.n_buckets;
+  p.B = B;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.T = T;
+  p.G = G;
+  const double scale = d->scale > 0.f ? (double)d->scale : 1.0 / sqrt((double)d->d);
+  p.scale = (float)scale;
+  p.scale_log2 = (float)(scale * 1.4426950408889634074);
+  int tmo = d->timeout_ms;
+  if (tmo <= 0) {
+    const char* env = getenv("NSA_SEL_TIMEOUT_MS");
+    tmo = env ? atoi(env) : 0;
+    if (tmo <= 0) tmo = 2000;
+  }
+  p.timeout_ns = (unsigned long long)tmo * 1000000ull;
+  int grid = sm;
+  if (d->max_ctas > 0 && d->max_ctas < grid) grid = d->max_ctas;
+  void* args[] = {&tmQ, &tmDO, &tmK, &tmV, &p};
+  e = cudaLaunchKernel(reinterpret_cast<const void*>(&nsa::bwd::nsa_bwd_kernel), dim3(grid),
+                       dim3(nsa::bwd::kThreads), args, nsa::bwd::kSmemBytes, st);
+  if (e != cudaSuccess) return cuda_fail(e, "backward kernel launch");
+  g_last_error[0] = '\0';
+  return NSA_OK;
+}
+
 }  // namespace
 
 extern "C" {
+
+int64_t nsa_sel_backward_workspace_bytes(const nsa_sel_bwd_desc* desc) {
+  BwdLayout L;
+  if (bwd_layout(desc, &L) != NSA_OK) return -1;
+  return (int64_t)L.total;
+}
+
+int nsa_sel_backward(const nsa_sel_bwd_desc* desc, nsa_stream_t stream) { return backward(desc, stream); }
 
 int nsa_sel_run_host(const nsa_sel_desc* desc, const nsa_sel_host_io* io, nsa_stream_t stream) {
   return run_host(desc, io, stream);

@@ -58,5 +58,57 @@ def select_blocks(Q: torch.Tensor, K: torch.Tensor, n_sel: int, l_prime: int = 6
     return _C.select_blocks(Q, K, int(n_sel), int(l_prime), int(cmp_block), int(cmp_stride))
 
 
+def backward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, sel: torch.Tensor, O: torch.Tensor,
+             LSE: torch.Tensor, dO: torch.Tensor, l_prime: int = 64, scale: float = 0.0
+             ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Gradients (fp32 dQ, dK, dV) of the selected-branch forward for the upstream gradient dO,
+    given that forward's O (bf16 or fp32) and LSE.  Per-token selection (sel [B,Hkv,T,KSEL]),
+    d = 128, G = Hq/Hkv in {8, 16} (nsa_sel_backward; the reference has no backward pass).  The
+    workspace comes from torch's caching allocator; the library allocates nothing."""
+    from . import capi
+
+    for name, t in (("Q", Q), ("K", K), ("V", V), ("dO", dO)):
+        if t.dtype != torch.bfloat16 or not t.is_cuda or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous bf16 CUDA tensor")
+    if O.dtype not in (torch.bfloat16, torch.float32) or not O.is_contiguous():
+        raise ValueError("O must be a contiguous bf16 or fp32 tensor")
+    if LSE.dtype != torch.float32 or not LSE.is_contiguous():
+        raise ValueError("LSE must be a contiguous fp32 tensor")
+    sel = sel.to(torch.int32).contiguous()
+    B, Hq, T, d = Q.shape
+    Hkv = K.shape[1]
+    dq = torch.zeros(B, Hq, T, d, device=Q.device, dtype=torch.float32)
+    dk = torch.zeros(B, Hkv, T, d, device=Q.device, dtype=torch.float32)
+    dv = torch.zeros_like(dk)
+    desc = capi.make_bwd_desc(
+        q=Q.data_ptr(), k=K.data_ptr(), v=V.data_ptr(), sel=sel.data_ptr(), o=O.data_ptr(), lse=LSE.data_ptr(),
+        d_o=dO.data_ptr(), dq=dq.data_ptr(), dk=dk.data_ptr(), dv=dv.data_ptr(), batch=B, heads_q=Hq,
+        heads_kv=Hkv, seq_len=T, d=d, n_sel=sel.shape[-1], block_size=int(l_prime),
+        o_dtype=capi.DTYPE_BF16 if O.dtype == torch.bfloat16 else capi.DTYPE_F32, scale=float(scale))
+    ws = torch.empty(capi.backward_workspace_bytes(desc), device=Q.device, dtype=torch.uint8)
+    desc.workspace = ws.data_ptr()
+    capi.backward(desc, torch.cuda.current_stream(Q.device).cuda_stream)
+    return dq, dk, dv
+
+
+class SelectedAttention(torch.autograd.Function):
+    """Selected-branch attention with its backward: ``O = SelectedAttention.apply(Q, K, V, sel)``
+    (per-token selection, l_prime = 64) returns bf16 O and supports ``O.backward(dO)``; Q, K, V
+    receive bf16 gradients computed by nsa_sel_backward."""
+
+    @staticmethod
+    def forward(ctx, Q, K, V, sel, l_prime: int = 64):
+        O, LSE = forward_lse(Q, K, V, sel, l_prime, 1)
+        ctx.save_for_backward(Q, K, V, sel, O, LSE)
+        ctx.l_prime = l_prime
+        return O
+
+    @staticmethod
+    def backward(ctx, dO):
+        Q, K, V, sel, O, LSE = ctx.saved_tensors
+        dq, dk, dv = backward(Q, K, V, sel, O, LSE, dO.contiguous().to(torch.bfloat16), ctx.l_prime)
+        return dq.to(Q.dtype), dk.to(K.dtype), dv.to(V.dtype), None, None
+
+
 def library_version() -> int:
     return int(_C.library_version())

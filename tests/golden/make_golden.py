@@ -141,17 +141,71 @@ def nsa_full_cases(out_dir, nsa_forward, compress_kv):
         print("wrote", name)
 
 
+def backward_cases(out_dir, ref_selected):
+    """Gradients of the selected branch (the reference has no backward: its README (2).md:85):
+    autograd through ``ref_only.ref_selected`` in fp64 (ref_only.py:2-20) with a seeded upstream
+    gradient dO, per-token selection (BQ = 1), d = 128, G = 16 and 8.  Stored per case: SHA-256 of
+    the bf16 Q, K, V and dO, the selection rows, and for each of dQ, dK, dV three full-tensor fp64
+    checksums and 64 seeded fp64 rows."""
+    cases = [
+        # name, B, Hq, Hkv, T, D, n, l_prime, seed, edit
+        ("bwd_rule0_g16", 1, 16, 1, 512, 128, 8, 64, 300, None),
+        ("bwd_rule0_g8_b2", 2, 16, 2, 384, 128, 4, 64, 301, None),
+        ("bwd_edges_t300", 1, 16, 2, 300, 128, 6, 64, 302, "edges"),
+        ("bwd_lp128", 1, 16, 1, 512, 128, 3, 128, 303, None),
+        ("bwd_bigrow", 1, 16, 1, 256, 128, 4, 64, 304, "bigrow"),
+        ("bwd_lp256", 1, 16, 1, 600, 128, 2, 256, 305, None),
+    ]
+    for name, B, Hq, Hkv, T, D, n, lp, seed, edit in cases:
+        q, k, v = qkv(B, Hq, Hkv, T, D, D, seed)
+        if edit == "bigrow":  # make_testset.py:24-25: a large-magnitude query row
+            q = q.clone()
+            q[..., 0, :] = (q[..., 0, :].float() * 50.0).to(torch.bfloat16)
+        sel = indices.rule0(B, Hkv, T, n, lp, seed=seed)
+        if edit == "edges":  # repeats, padding in the middle, the scratch id n_blk, future blocks
+            n_blk = (T + lp - 1) // lp
+            t = np.arange(T)
+            sel[..., t % 7 == 3, 1] = sel[..., t % 7 == 3, 0]
+            sel[..., t % 5 == 1, n - 1] = -1
+            sel[..., t % 11 == 4, 2] = n_blk
+            fut = t % 13 == 6
+            sel[..., fut, 3] = np.minimum(n_blk - 1, t[fut] // lp + 2)
+        g = torch.Generator().manual_seed(seed + 1000)
+        do = torch.randn(B, Hq, T, D, generator=g).to(torch.bfloat16)
+        Q, K, V = (x.double().requires_grad_() for x in (q, k, v))
+        O = ref_selected(Q, K, V, torch.from_numpy(sel), lp, 1)
+        O.backward(do.double())
+        rec = dict(kind="ref_selected_backward", B=B, Hq=Hq, Hkv=Hkv, T=T, dqk=D, dv=D, LP=lp, BQ=1, n_sel=n,
+                   seed=seed, big_row=int(edit == "bigrow"), sha256=digest(q, k, v), sha256_do=digest(do),
+                   sel=sel.astype(np.int32))
+        rng = np.random.Generator(np.random.PCG64(seed))
+        for key, grad, H in (("dq", Q.grad, Hq), ("dk", K.grad, Hkv), ("dv", V.grad, Hkv)):
+            x = grad.numpy()
+            rows = np.stack([rng.integers(0, B, 64), rng.integers(0, H, 64), rng.integers(0, T, 64)], 1)
+            rec[key + "_checksums"] = checksums(x, 1234)
+            rec[key + "_rows"] = rows.astype(np.int32)
+            rec[key + "_vals"] = x[rows[:, 0], rows[:, 1], rows[:, 2]].astype(np.float64)
+            rec[key + "_absmax"] = np.abs(x).max()
+        np.savez_compressed(os.path.join(out_dir, name + ".npz"), **{k2: np.asarray(v2) for k2, v2 in rec.items()})
+        print("wrote", name)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="directory holding ref_only.py and nsa_reference.py")
     ap.add_argument("--out", default=HERE)
-    ap.add_argument("--only", choices=["selected", "nsa_full"], default=None, help="generate one group of fixtures")
+    ap.add_argument("--only", choices=["selected", "nsa_full", "backward"], default=None,
+                    help="generate one group of fixtures")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     from nsa_reference import compress_kv, nsa_forward  # noqa: E402
     from ref_only import ref_selected  # noqa: E402
 
     torch.set_num_threads(max(1, os.cpu_count() or 1))
+    if args.only in (None, "backward"):
+        backward_cases(args.out, ref_selected)
+    if args.only == "backward":
+        return
     if args.only != "selected":
         nsa_full_cases(args.out, nsa_forward, compress_kv)
     if args.only == "nsa_full":

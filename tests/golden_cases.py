@@ -15,7 +15,12 @@ GOLDEN_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 def case_names() -> List[str]:
     """Selected-branch fixtures (ref_selected / the selected branch of nsa_forward)."""
     return sorted(os.path.splitext(os.path.basename(p))[0] for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz"))
-                  if not os.path.basename(p).startswith("nsa_full_"))
+                  if not os.path.basename(p).startswith(("nsa_full_", "bwd_")))
+
+
+def bwd_case_names() -> List[str]:
+    """Backward fixtures: autograd of ref_selected with a seeded upstream gradient."""
+    return sorted(os.path.splitext(os.path.basename(p))[0] for p in glob.glob(os.path.join(GOLDEN_DIR, "bwd_*.npz")))
 
 
 def full_case_names() -> List[str]:
@@ -44,6 +49,17 @@ def load(name: str) -> Dict:
     if h.hexdigest() != str(c["sha256"]):
         raise RuntimeError(f"{name}: regenerated inputs differ from the fixture's (torch generator changed?)")
     c["q"], c["k"], c["v"] = q, k, v
+    return c
+
+
+def load_bwd(name: str) -> Dict:
+    """A backward fixture with its regenerated inputs, including the upstream gradient d_o."""
+    c = load(name)
+    g = torch.Generator().manual_seed(c["seed"] + 1000)
+    d_o = torch.randn(c["B"], c["Hq"], c["T"], c["dqk"], generator=g).to(torch.bfloat16)
+    if hashlib.sha256(d_o.contiguous().view(torch.int16).numpy().tobytes()).hexdigest() != str(c["sha256_do"]):
+        raise RuntimeError(f"{name}: regenerated dO differs from the fixture's")
+    c["d_o"] = d_o
     return c
 
 

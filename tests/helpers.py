@@ -75,3 +75,36 @@ def compare(o_dev: torch.Tensor, lse_dev: Optional[torch.Tensor], o_ref: np.ndar
         res["lse_max_rel"] = float(rel.max()) if rel.size else 0.0
         assert res["lse_max_rel"] <= lse_rtol, f"LSE mismatch {res}"
     return res
+
+
+def run_backward_capi(q, k, v, sel, d_o, o, lse, *, l_prime: int = 64, scale: float = 0.0, grads=None,
+                      timeout_ms: int = 0):
+    """nsa_sel_backward on torch buffers through the C ABI; returns (dQ, dK, dV, err) device
+    tensors.  ``grads`` = (dq, dk, dv) fp32 buffers to accumulate into (zeros if None)."""
+    dev = torch.device("cuda")
+    q, k, v, d_o = (x.to(dev).contiguous() for x in (q, k, v, d_o))
+    sel = sel.to(dev, torch.int32).contiguous() if torch.is_tensor(sel) else torch.from_numpy(
+        np.ascontiguousarray(sel, dtype=np.int32)).to(dev)
+    B, Hq, T, d = q.shape
+    Hkv = k.shape[1]
+    if grads is None:
+        grads = (torch.zeros(B, Hq, T, d, device=dev), torch.zeros(B, Hkv, T, d, device=dev),
+                 torch.zeros(B, Hkv, T, d, device=dev))
+    dq, dk, dv = grads
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    desc = capi.make_bwd_desc(
+        q=q.data_ptr(), k=k.data_ptr(), v=v.data_ptr(), sel=sel.data_ptr(), o=o.data_ptr(), lse=lse.data_ptr(),
+        d_o=d_o.data_ptr(), dq=dq.data_ptr(), dk=dk.data_ptr(), dv=dv.data_ptr(), err=err.data_ptr(), batch=B,
+        heads_q=Hq, heads_kv=Hkv, seq_len=T, d=d, n_sel=sel.shape[-1], block_size=l_prime,
+        o_dtype=capi.DTYPE_BF16 if o.dtype == torch.bfloat16 else capi.DTYPE_F32, scale=scale,
+        timeout_ms=timeout_ms)
+    ws = torch.empty(capi.backward_workspace_bytes(desc), dtype=torch.uint8, device=dev)
+    desc.workspace = ws.data_ptr()
+    capi.backward(desc, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    return dq, dk, dv, err
+
+
+def scaled_err(x: np.ndarray, ref: np.ndarray) -> float:
+    """max |x - ref| / max |ref| (the reference validate.py's metric, validate.py:12-28)."""
+    return float(np.abs(np.asarray(x, np.float64) - ref).max() / max(np.abs(ref).max(), 1e-30))

@@ -30,23 +30,26 @@ def test_struct_layout_matches_header(tmp_path):
     fields = [f for f, _ in capi.NsaSelDesc._fields_]
     pfields = [f for f, _ in capi.NsaSelPlanInfo._fields_]
     hfields = [f for f, _ in capi.NsaSelHostIO._fields_]
+    bfields = [f for f, _ in capi.NsaSelBwdDesc._fields_]
     src = tmp_path / "layout.c"
     lines = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{capi.HEADER_PATH}"', "int main(void) {",
              'printf("%zu\\n", sizeof(nsa_sel_desc));', 'printf("%zu\\n", sizeof(nsa_sel_plan_info));',
-             'printf("%zu\\n", sizeof(nsa_sel_host_io));']
+             'printf("%zu\\n", sizeof(nsa_sel_host_io));', 'printf("%zu\\n", sizeof(nsa_sel_bwd_desc));']
     lines += [f'printf("%zu\\n", offsetof(nsa_sel_desc, {f}));' for f in fields]
     lines += [f'printf("%zu\\n", offsetof(nsa_sel_plan_info, {f}));' for f in pfields]
     lines += [f'printf("%zu\\n", offsetof(nsa_sel_host_io, {f}));' for f in hfields]
+    lines += [f'printf("%zu\\n", offsetof(nsa_sel_bwd_desc, {f}));' for f in bfields]
     lines += ["return 0; }"]
     src.write_text("\n".join(lines))
     exe = tmp_path / "layout"
     subprocess.run(["gcc", "-o", str(exe), str(src)], check=True)
     vals = [int(x) for x in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split()]
     assert vals[0] == ctypes.sizeof(capi.NsaSelDesc) and vals[1] == ctypes.sizeof(capi.NsaSelPlanInfo)
-    assert vals[2] == ctypes.sizeof(capi.NsaSelHostIO)
-    got = vals[3:]
+    assert vals[2] == ctypes.sizeof(capi.NsaSelHostIO) and vals[3] == ctypes.sizeof(capi.NsaSelBwdDesc)
+    got = vals[4:]
     want = [getattr(capi.NsaSelDesc, f).offset for f in fields] + [getattr(capi.NsaSelPlanInfo, f).offset for f in pfields]
     want += [getattr(capi.NsaSelHostIO, f).offset for f in hfields]
+    want += [getattr(capi.NsaSelBwdDesc, f).offset for f in bfields]
     assert got == want
 
 
@@ -191,3 +194,46 @@ def test_host_path_validation():
     assert lib.nsa_sel_run_host(ctypes.byref(d), ctypes.byref(io), None) == capi.NSA_ERR_UNSUPPORTED
     io.token_slices = -1
     assert lib.nsa_sel_run_host(ctypes.byref(_desc()), ctypes.byref(io), None) == capi.NSA_ERR_INVALID_ARG
+
+
+def _bwd(**kw):
+    base = dict(q=16, k=16, v=16, sel=16, o=16, lse=16, d_o=16, dq=16, dk=16, dv=16, workspace=16, batch=1,
+                heads_q=64, heads_kv=4, seq_len=65536, d=128, n_sel=16, block_size=64)
+    base.update(kw)
+    return capi.make_bwd_desc(**base)
+
+
+def test_backward_workspace_bytes():
+    """Row sums (B*Hq*T floats) + index: 4 bucket arrays, token entries (B*Hkv*T*KSEL*l'/64 at
+    most) and 16-byte work items, each region 16-byte aligned."""
+    n = capi.backward_workspace_bytes(_bwd())
+    rows, buckets, pairs = 64 * 65536, 4 * 1024, 4 * 65536 * 16
+    expect = rows * 4 + 3 * buckets * 4 + (buckets + 1) * 4 + pairs * 4 + (pairs // 128 + buckets) * 16
+    assert expect <= n <= expect + 7 * 16
+    assert capi.backward_workspace_bytes(_bwd(block_size=128, n_sel=4)) < n
+
+
+@pytest.mark.parametrize("kw, code", [
+    (dict(heads_q=32, heads_kv=8), capi.NSA_ERR_UNSUPPORTED),   # G = 4
+    (dict(d=64), capi.NSA_ERR_UNSUPPORTED),
+    (dict(block_size=96), capi.NSA_ERR_UNSUPPORTED),
+    (dict(heads_q=65), capi.NSA_ERR_INVALID_ARG),
+    (dict(n_sel=0), capi.NSA_ERR_INVALID_ARG),
+    (dict(o_dtype=7), capi.NSA_ERR_INVALID_ARG),
+])
+def test_backward_validation(kw, code):
+    """The description is checked before any device call (this runs without a GPU)."""
+    with pytest.raises(capi.NsaSelError) as ei:
+        capi.backward(_bwd(**kw))
+    assert ei.value.code == code
+    with pytest.raises(capi.NsaSelError):  # the size query reports -1 for the same descriptions
+        capi.backward_workspace_bytes(_bwd(**kw))
+
+
+def test_backward_rejects_null_and_misaligned_pointers_before_touching_a_device():
+    with pytest.raises(capi.NsaSelError) as ei:
+        capi.backward(_bwd(dq=None))
+    assert ei.value.code == capi.NSA_ERR_INVALID_ARG
+    with pytest.raises(capi.NsaSelError) as ei:
+        capi.backward(_bwd(dk=24))
+    assert ei.value.code == capi.NSA_ERR_INVALID_ARG
