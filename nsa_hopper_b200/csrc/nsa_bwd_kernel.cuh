@@ -9,22 +9,26 @@
 //     dQ_i = s sum_j dS_ij k_j    dK_j = s sum_i dS_ij q_i    dV_j = sum_i P_ij dO_i
 //
 // Layout of the work (B200-first, not a restatement of any reference code): the scatter onto
-// K/V is inverted.  An index lists, per (b*Hkv + kvh, 64-key sub-block u), the tokens whose
-// selection row holds u (set semantics, visible keys only; built on the device with atomic
-// counters, so in no fixed order within a sub-block); a work item is one such
-// sub-block with up to kItemTokens of its tokens.  A CTA loads K_u, V_u once (TMA, 16 KB each)
-// and walks the item's tokens in groups of 128 / G (128 query rows), each gathered by TMA
-// (one 2 KB box of G heads per token and 64-dim slice), with five tcgen05 UMMAs per group:
+// K/V is inverted.  An index lists, per (b*Hkv + kvh, token window, 64-key sub-block u), the tokens
+// of the window whose selection row holds u (set semantics, visible keys only; built on the device
+// with atomic counters, so in no fixed order within a bucket); a work item is one bucket's
+// sub-block with up to kItemTokens of its tokens.  Items are ordered by window, so the CTAs sweep
+// the tokens of one window at a time and its Q, dO and dQ rows stay in L2.  A CTA loads K_u, V_u
+// once per item (TMA, 16 KB each) and walks the item's tokens in groups of 128 / G (128 query
+// rows), each gathered by TMA (one box of G heads per token and 64-dim slice, issued by one lane
+// per token), with five tcgen05 UMMAs per group:
 //     S  [128 rows x 64 keys]  = Q_g  . K_u^T        (A K-major, B K-major)
 //     dP [128 rows x 64 keys]  = dO_g . V_u^T        (A K-major, B K-major)
 //     dV^T [128 d x 64 keys]  += dO_g^T . P          (A MN-major, B MN-major; TMEM accumulator)
 //     dK^T [128 d x 64 keys]  += Q_g^T . dS          (A MN-major, B MN-major; TMEM accumulator)
-//     dQ [128 rows x 128 d]    = dS . K_u            (A K-major, B MN-major)
+//     dQ [128 rows x 128 d]    = dS . K_u            (A K-major, B MN-major; two TMEM buffers)
 // A softmax-gradient warpgroup (one TMEM lane = one query row per thread) turns S and dP into
-// P and dS (bf16, written into shared memory in the UMMA's SW128 layout) and adds each dQ row
-// into the fp32 dQ with 16-byte vector reductions.  After an item's last group the same
-// warpgroup adds dK^T and dV^T into the fp32 dK, dV (reductions: a sub-block's tokens may span
-// several items).  dQ, dK, dV must be zeroed by the caller.
+// P and dS (bf16, written into shared memory in the UMMA's SW128 layout).  While the UMMAs of
+// group n run, it moves dQ of group n - 1 out of TMEM: scaled into SW128 staging tiles and added
+// into the fp32 dQ by TMA reduce-adds (whole 128-byte rows at the L2, one instruction per token
+// and 32 dimensions).  After an item's last group the same warpgroup adds dK^T and dV^T into
+// the fp32 dK, dV (coalesced reductions: a sub-block's tokens span several items).  dQ, dK, dV
+// must be zeroed by the caller.
 //
 // Roles: warp 0 TMA producer, warp 1 MMA issuer (owns TMEM), warps 2-5 softmax-gradient.
 // Every mbarrier wait is bounded (nsa::Waiter); on a timeout all roles stop, in-flight TMA
@@ -45,8 +49,8 @@ constexpr int kRows = 128;            // query rows per group (M)
 constexpr int kItemTokens = 128;      // tokens per work item (upper bound)
 constexpr int kThreads = 192;
 constexpr int kTmemCols = 512;
-// TMEM columns
-constexpr uint32_t kTmS = 0, kTmDP = 64, kTmDQ = 128, kTmDK = 256, kTmDV = 320;
+// TMEM columns: S, dP, two dQ buffers (group n uses buffer n & 1), dK^T, dV^T
+constexpr uint32_t kTmS = 0, kTmDP = 64, kTmDQ = 128, kTmDK = 384, kTmDV = 448;
 // Shared-memory layout (bytes from a 1024-aligned base)
 constexpr uint32_t kKVSlice = kKeys * 128;                 // one 64-dim slice of a 64-key tile: 8 KB
 constexpr uint32_t kKVTile = 2 * kKVSlice;                 // K_u or V_u: 16 KB
@@ -56,22 +60,26 @@ constexpr uint32_t kOffK = 0, kOffV = kKVTile;
 constexpr uint32_t kOffQ = 2 * kKVTile;                    // [buf][Q, dO]
 constexpr uint32_t kOffP = kOffQ + 4 * kRowTile;           // P [128 rows x 64 keys] bf16, SW128
 constexpr uint32_t kOffDS = kOffP + kRows * 128;           // dS, same layout
-constexpr uint32_t kOffBar = kOffDS + kRows * 128;
+// dQ staging: per softmax-gradient warp, its 32 rows x 64 fp32 dimensions (half of d) as two
+// SW128 [32 rows x 128 B] tiles, the source of the TMA reduce-add into dQ
+constexpr uint32_t kStageWarp = 2 * 32 * 128;              // 8 KB
+constexpr uint32_t kOffStage = kOffDS + kRows * 128;
+constexpr uint32_t kOffBar = kOffStage + 4 * kStageWarp;
 
 struct Bars {
-  uint64_t kv_full, kv_empty, q_full[2], q_empty[2], s_full, s_empty, p_full, pd_empty, dq_full, dq_empty,
+  uint64_t kv_full, kv_empty, q_full[2], q_empty[2], s_full, s_empty, p_full, pd_empty, dq_full[2], dq_empty[2],
       acc_full, acc_empty, drain;
   uint32_t tmem_base;
   int abort_flag;
 };
 constexpr uint32_t kSmemBytes = kOffBar + sizeof(Bars) + 1024;
+static_assert(kSmemBytes <= 232448, "shared memory of the backward kernel exceeds the per-block limit");
 
 struct Params {
-  const int32_t* tokens;  // inverse index: token ids, grouped by (bkv, sub-block)
+  const int32_t* tokens;  // inverse index: token ids, grouped by (bkv, token window, sub-block)
   const int32_t* items;   // [n_items][4]: bkv, sub-block u, first entry in `tokens`, count (<= kItemTokens)
   const float* lse;       // [B, Hq, T]
   const float* delta;     // [B, Hq, T]: rowsum(dO * O)
-  float* dq;              // [B, Hq, T, 128] fp32 (accumulated)
   float* dk;              // [B, Hkv, T, 128] fp32 (accumulated)
   float* dv;
   int32_t* err;
@@ -87,10 +95,58 @@ constexpr uint32_t kIdescDQ = ptx::idesc_bf16_f32(128, 128, false, true);
 
 __device__ __forceinline__ int group_count(int count, int R) { return (count + R - 1) / R; }
 
+// dQ of one group (TMEM buffer `tm_dq`, lane = query row of this warp) into the fp32 dQ: each half
+// of d goes through this warp's staging tiles (scaled, SW128) and one TMA reduce-add per (token,
+// 32 dimensions).  `t` is the token of this lane's row (-1: padding row); rows s*G .. s*G+G-1 of
+// the warp are the G heads of one token.  Releases the TMEM buffer once it has been read.
+__device__ __forceinline__ bool dq_flush(const Waiter& w, Bars* bars, uint32_t j, uint32_t tm_dq, uint8_t* stage,
+                                         const CUtensorMap* tmDQ, int t, int b, int kvh, int G, float scale,
+                                         int lane) {
+  if (!w.wait(&bars->dq_full[j & 1], (j >> 1) & 1)) return false;
+  ptx::tc_fence_after();
+  const uint32_t st0 = ptx::smem_u32(stage);
+#pragma unroll 1
+  for (int half = 0; half < 2; ++half) {
+    float a[32], c[32];
+    ptx::tmem_ld32(tm_dq + half * 64, a);
+    ptx::tmem_ld32(tm_dq + half * 64 + 32, c);
+    ptx::tmem_wait_ld();
+    if (half == 1) {
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&bars->dq_empty[j & 1]);
+    }
+    // the previous reduce has finished reading the staging tiles
+    if (lane == 0) ptx::bulk_wait_read<0>();
+    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {  // 16-byte chunk k of the row, at SW128 position k ^ (row & 7)
+      const uint32_t off = (uint32_t)lane * 128 + (uint32_t)((k ^ (lane & 7)) << 4);
+      asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(st0 + off), "f"(a[4 * k] * scale),
+                   "f"(a[4 * k + 1] * scale), "f"(a[4 * k + 2] * scale), "f"(a[4 * k + 3] * scale)
+                   : "memory");
+      asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(st0 + 4096 + off), "f"(c[4 * k] * scale),
+                   "f"(c[4 * k + 1] * scale), "f"(c[4 * k + 2] * scale), "f"(c[4 * k + 3] * scale)
+                   : "memory");
+    }
+    ptx::fence_proxy_async_smem();
+    __syncwarp();
+    for (int s = 0; s < 32 / G; ++s) {
+      const int ts = __shfl_sync(0xffffffffu, t, s * G);
+      if (lane == 0 && ts >= 0) {
+        ptx::tma_reduce_add_4d(tmDQ, stage + s * G * 128, half * 64, ts, kvh * G, b);
+        ptx::tma_reduce_add_4d(tmDQ, stage + 4096 + s * G * 128, half * 64 + 32, ts, kvh * G, b);
+      }
+    }
+    if (lane == 0) ptx::bulk_commit();
+  }
+  return true;
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     nsa_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
                    const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
-                   const __grid_constant__ Params p) {
+                   const __grid_constant__ CUtensorMap tmDQ, const __grid_constant__ Params p) {
   uint8_t* smem = smem_base();
   Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -103,13 +159,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < 2; ++s) {
       ptx::mbar_init(&bars->q_full[s], 1);
       ptx::mbar_init(&bars->q_empty[s], 1);
+      ptx::mbar_init(&bars->dq_full[s], 1);
+      ptx::mbar_init(&bars->dq_empty[s], 4);
     }
     ptx::mbar_init(&bars->s_full, 1);
     ptx::mbar_init(&bars->s_empty, 4);
     ptx::mbar_init(&bars->p_full, 4);
     ptx::mbar_init(&bars->pd_empty, 1);
-    ptx::mbar_init(&bars->dq_full, 1);
-    ptx::mbar_init(&bars->dq_empty, 4);
     ptx::mbar_init(&bars->acc_full, 1);
     ptx::mbar_init(&bars->acc_empty, 4);
     ptx::mbar_init(&bars->drain, 1);
@@ -126,6 +182,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::prefetch_tmap(&tmDO);
     ptx::prefetch_tmap(&tmK);
     ptx::prefetch_tmap(&tmV);
+    ptx::prefetch_tmap(&tmDQ);
   }
   if (warp == 1) {
     ptx::tmem_alloc(&bars->tmem_base, kTmemCols);
@@ -138,41 +195,60 @@ __global__ void __launch_bounds__(kThreads, 1)
   const Waiter w{&bars->abort_flag, p.err, p.timeout_ns};
 
   if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      const uint64_t pol_kv = ptx::policy_evict_last();
-      const uint64_t pol_q = ptx::policy_evict_first();
-      uint32_t m = 0, n = 0;  // items, groups issued
-      bool ok = true;
-      for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++m) {
-        const int4 item = __ldg(reinterpret_cast<const int4*>(p.items) + it);
-        const int bkv = item.x, u = item.y, first = item.z, count = item.w;
-        const int b = bkv / p.Hkv, kvh = bkv - b * p.Hkv;
-        if (m > 0 && !w.wait(&bars->kv_empty, (m - 1) & 1)) { ok = false; break; }
-        ptx::mbar_arrive_expect_tx(&bars->kv_full, 2 * kKVTile);
-        ptx::tma_load_4d(smem + kOffK, &tmK, &bars->kv_full, 0, u * kKeys, 0, bkv, pol_kv);
-        ptx::tma_load_4d(smem + kOffV, &tmV, &bars->kv_full, 0, u * kKeys, 0, bkv, pol_kv);
-        const int ng = group_count(count, R);
-        for (int g = 0; g < ng; ++g, ++n) {
-          const uint32_t buf = n & 1;
-          if (n >= 2 && !w.wait(&bars->q_empty[buf], ((n >> 1) - 1) & 1)) { ok = false; break; }
-          const int nt = min(R, count - g * R);
-          ptx::mbar_arrive_expect_tx(&bars->q_full[buf], (uint32_t)(nt * 2 * p.G * kD * 2));
-          uint8_t* qd = smem + kOffQ + buf * 2 * kRowTile;
-          for (int s = 0; s < nt; ++s) {
-            const int t = __ldg(p.tokens + first + g * R + s);
-            for (int c = 0; c < 2; ++c) {
-              const uint32_t off = c * kRowSlice + (uint32_t)(s * p.G) * 128;
-              ptx::tma_load_4d(qd + off, &tmQ, &bars->q_full[buf], c * 64, t, kvh * p.G, b, pol_q);
-              ptx::tma_load_4d(qd + kRowTile + off, &tmDO, &bars->q_full[buf], c * 64, t, kvh * p.G, b, pol_q);
-            }
-          }
+    // ------------------------------------------------------------------ TMA producer (whole warp:
+    // lane 0 waits and arms the barriers, lane s loads token s of a group)
+    const uint64_t pol_kv = ptx::policy_evict_last();
+    const uint64_t pol_q = ptx::policy_evict_first();
+    uint32_t kv_issued = 0, q_issued = 0;
+    bool ok = true;
+    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+      const int4 item = __ldg(reinterpret_cast<const int4*>(p.items) + it);
+      const int bkv = item.x, u = item.y, first = item.z, count = item.w;
+      const int b = bkv / p.Hkv, kvh = bkv - b * p.Hkv;
+      if (lane == 0) {
+        if (kv_issued > 0 && !w.wait(&bars->kv_empty, (kv_issued - 1) & 1)) {
+          ok = false;
+        } else {
+          ptx::mbar_arrive_expect_tx(&bars->kv_full, 2 * kKVTile);
+          ptx::tma_load_4d(smem + kOffK, &tmK, &bars->kv_full, 0, u * kKeys, 0, bkv, pol_kv);
+          ptx::tma_load_4d(smem + kOffV, &tmV, &bars->kv_full, 0, u * kKeys, 0, bkv, pol_kv);
         }
       }
-      // Drain: the most recent load into each buffer has landed.
-      if (m > 0) w.wait_drain(&bars->kv_full, (m - 1) & 1);
-      for (uint32_t back = 1; back <= 2 && back <= n; ++back) {
-        const uint32_t k = n - back;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      ++kv_issued;
+      const int ng = group_count(count, R);
+      for (int g = 0; g < ng; ++g) {
+        const uint32_t n = q_issued, buf = n & 1;
+        const int nt = min(R, count - g * R);
+        // token ids of the group, one per lane, in flight while lane 0 waits for the buffer
+        const int t = lane < nt ? __ldg(p.tokens + first + g * R + lane) : 0;
+        if (lane == 0) {
+          if (n >= 2 && !w.wait(&bars->q_empty[buf], ((n >> 1) - 1) & 1))
+            ok = false;
+          else
+            ptx::mbar_arrive_expect_tx(&bars->q_full[buf], (uint32_t)(nt * 2 * p.G * kD * 2));
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        ++q_issued;
+        if (lane < nt) {
+          uint8_t* qd = smem + kOffQ + buf * 2 * kRowTile;
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const uint32_t off = c * kRowSlice + (uint32_t)(lane * p.G) * 128;
+            ptx::tma_load_4d(qd + off, &tmQ, &bars->q_full[buf], c * 64, t, kvh * p.G, b, pol_q);
+            ptx::tma_load_4d(qd + kRowTile + off, &tmDO, &bars->q_full[buf], c * 64, t, kvh * p.G, b, pol_q);
+          }
+        }
+        __syncwarp();
+      }
+    }
+    // Drain: the most recent load into each buffer has landed.
+    if (lane == 0) {
+      if (kv_issued > 0) w.wait_drain(&bars->kv_full, (kv_issued - 1) & 1);
+      for (uint32_t back = 1; back <= 2 && back <= q_issued; ++back) {
+        const uint32_t k = q_issued - back;
         w.wait_drain(&bars->q_full[k & 1], (k >> 1) & 1);
       }
     }
@@ -189,7 +265,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int ng = group_count(item.w, R);
         if (!w.wait(&bars->kv_full, m & 1)) { ok = false; break; }
         for (int g = 0; g < ng; ++g, ++n) {
-          const uint32_t buf = n & 1;
+          const uint32_t buf = n & 1, dqb = n & 1;
           const uint32_t q_base = ptx::smem_u32(smem + kOffQ + buf * 2 * kRowTile);
           const uint32_t do_base = q_base + kRowTile;
           if (!w.wait(&bars->q_full[buf], (n >> 1) & 1)) { ok = false; break; }
@@ -213,8 +289,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!w.wait(&bars->p_full, n & 1)) { ok = false; break; }
           // the accumulators of the previous item have been read out
           if (g == 0 && m >= 1 && !w.wait(&bars->acc_empty, (m - 1) & 1)) { ok = false; break; }
-          // dQ of the previous group has been read out
-          if (n >= 1 && !w.wait(&bars->dq_empty, (n - 1) & 1)) { ok = false; break; }
+          // dQ buffer dqb was read out (group n - 2)
+          if (n >= 2 && !w.wait(&bars->dq_empty[dqb], ((n >> 1) - 1) & 1)) { ok = false; break; }
           ptx::tc_fence_after();
 #pragma unroll
           for (int j = 0; j < kRows / 16; ++j) {  // K = query rows, 16 per step
@@ -227,12 +303,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
 #pragma unroll
           for (int j = 0; j < kKeys / 16; ++j) {  // K = keys, 16 per step
-            ptx::umma_bf16(tmem + kTmDQ, ptx::sdesc_sw128(ds_base + j * 32, 16, 1024),
+            ptx::umma_bf16(tmem + kTmDQ + dqb * 128, ptx::sdesc_sw128(ds_base + j * 32, 16, 1024),
                            ptx::sdesc_sw128(k_base + j * 2048, kKVSlice, 1024), kIdescDQ, j > 0 ? 1u : 0u);
           }
           ptx::umma_commit(&bars->pd_empty);
           ptx::umma_commit(&bars->q_empty[buf]);
-          ptx::umma_commit(&bars->dq_full);
+          ptx::umma_commit(&bars->dq_full[dqb]);
         }
         if (!ok) break;
         ptx::umma_commit(&bars->kv_empty);
@@ -244,13 +320,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------------ softmax-gradient warpgroup
+    // Per group n: P and dS from S and dP; then dQ of group n - 1 (its UMMAs ran meanwhile) out of
+    // TMEM into the fp32 dQ; after an item's last group, dK and dV of the item.
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;  // TMEM lane: query row of S / dP / dQ, dimension of dK^T / dV^T
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
     const int slot = r / p.G, h = r - (r / p.G) * p.G;
     const float sl2 = p.scale_log2;
+    uint8_t* stage = smem + kOffStage + (uint32_t)quarter * kStageWarp;
     uint32_t m = 0, n = 0;
     bool dead = false;
+    int pend_t = -1, pend_b = 0, pend_kvh = 0;  // the group whose dQ is still in TMEM
     uint8_t* prow = smem + kOffP + (uint32_t)r * 128;
     uint8_t* dsrow = smem + kOffDS + (uint32_t)r * 128;
     for (int it = blockIdx.x; it < n_items && !dead; it += gridDim.x, ++m) {
@@ -259,12 +339,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int b = bkv / p.Hkv, kvh = bkv - b * p.Hkv;
       const int ng = group_count(count, R);
       const int key0 = u * kKeys;
+      const size_t row0 = ((size_t)b * p.Hq + (size_t)kvh * p.G + h) * p.T;
+      // the row data of group 0; later groups' are loaded one group ahead
+      int t_next = slot < count ? __ldg(p.tokens + first + slot) : -1;
+      float lse_next = t_next >= 0 ? __ldg(p.lse + row0 + t_next) * 1.4426950408889634f : 0.f;
+      float dlt_next = t_next >= 0 ? __ldg(p.delta + row0 + t_next) : 0.f;
       for (int g = 0; g < ng && !dead; ++g, ++n) {
-        const int ti = g * R + slot;
-        const int t = ti < count ? __ldg(p.tokens + first + ti) : -1;
-        const size_t row = ((size_t)b * p.Hq + (size_t)kvh * p.G + h) * p.T + (t < 0 ? 0 : t);
-        const float lse2 = t >= 0 ? __ldg(p.lse + row) * 1.4426950408889634f : 0.f;
-        const float dlt = t >= 0 ? __ldg(p.delta + row) : 0.f;
+        const int t = t_next;
+        const float lse2 = lse_next, dlt = dlt_next;
+        const int ti1 = (g + 1) * R + slot;
+        t_next = (g + 1 < ng && ti1 < count) ? __ldg(p.tokens + first + ti1) : -1;
         // keys of this sub-block visible to the row: key0 + j <= t
         const int nvis = t < 0 ? 0 : min(kKeys, t - key0 + 1);
         dead |= !w.wait(&bars->s_full, n & 1);
@@ -304,27 +388,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(&bars->p_full);
-        // dQ rows of this group
-        dead |= !w.wait(&bars->dq_full, n & 1);
-        if (dead) break;
-        ptx::tc_fence_after();
-        float* dqrow = p.dq + row * kD;
-#pragma unroll
-        for (int c = 0; c < kD / 32; ++c) {
-          float v[32];
-          ptx::tmem_ld32(tmem + lane_addr + kTmDQ + c * 32, v);
-          ptx::tmem_wait_ld();
-          if (t >= 0) {
-#pragma unroll
-            for (int q = 0; q < 8; ++q)
-              atomicAdd(reinterpret_cast<float4*>(dqrow + c * 32 + 4 * q),
-                        make_float4(v[4 * q] * p.scale, v[4 * q + 1] * p.scale, v[4 * q + 2] * p.scale,
-                                    v[4 * q + 3] * p.scale));
-          }
+        if (t_next >= 0) {
+          lse_next = __ldg(p.lse + row0 + t_next) * 1.4426950408889634f;
+          dlt_next = __ldg(p.delta + row0 + t_next);
         }
-        ptx::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&bars->dq_empty);
+        // dQ of the previous group
+        if (n >= 1) {
+          dead |= !dq_flush(w, bars, n - 1, tmem + lane_addr + kTmDQ + ((n - 1) & 1) * 128, stage, &tmDQ, pend_t,
+                            pend_b, pend_kvh, p.G, p.scale, lane);
+          if (dead) break;
+        }
+        pend_t = t;
+        pend_b = b;
+        pend_kvh = kvh;
       }
       if (dead) break;
       // dK^T, dV^T of the item: lane r = dimension, column j = key key0 + j
@@ -353,6 +429,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&bars->acc_empty);
     }
+    // dQ of the last group
+    if (!dead && n >= 1)
+      dq_flush(w, bars, n - 1, tmem + lane_addr + kTmDQ + ((n - 1) & 1) * 128, stage, &tmDQ, pend_t, pend_b,
+               pend_kvh, p.G, p.scale, lane);
+    // every reduce has completed before the CTA (and its shared memory) goes away
+    if (lane == 0) ptx::bulk_wait<0>();
+    __syncwarp();
   }
 
   ptx::tc_fence_before();
@@ -387,8 +470,12 @@ __global__ void delta_kernel(const __nv_bfloat16* __restrict__ d_o, const OT* __
 // The 64-key sub-blocks that token t of row bkv attends to: entry e of its selection row names
 // block e of l_prime keys (sub-blocks e*spb .. e*spb+spb-1); entries outside [0, n_blk), repeats
 // of an earlier entry and sub-blocks that start after t select nothing (the forward's rules).
+// Buckets are (bkv, token window, sub-block), windows of 2^win_shift tokens, so that the work
+// items of one window (consecutive in the item list, run at the same time by the CTAs) touch the
+// Q, dO and dQ rows of that window only: sized to stay in L2 while every sub-block the window's
+// tokens select is visited.
 struct IndexShape {
-  int n_bkv, T, KSEL, spb, n_blk, nsub, item_tokens;
+  int n_bkv, T, KSEL, spb, n_blk, nsub, item_tokens, win_shift, n_win;
 };
 
 template <bool kFill>
@@ -407,7 +494,7 @@ __global__ void index_rows_kernel(const int32_t* __restrict__ sel, IndexShape sh
     for (int s2 = 0; s2 < sh.spb; ++s2) {
       const int u = e * sh.spb + s2;
       if (u * kKeys > t) break;
-      const int bucket = bkv * sh.nsub + u;
+      const int bucket = (bkv * sh.n_win + (t >> sh.win_shift)) * sh.nsub + u;
       if (kFill) {
         const int pos = atomicAdd(fill + bucket, 1);
         tokens[tok_off[bucket] + pos] = t;
@@ -459,8 +546,8 @@ __global__ void index_scan_kernel(const int* __restrict__ counts, int n, int ite
 __global__ void index_items_kernel(IndexShape sh, const int* __restrict__ counts, const int* __restrict__ tok_off,
                                    const int* __restrict__ item_off, int4* __restrict__ items) {
   const int bucket = blockIdx.x * blockDim.x + threadIdx.x;
-  if (bucket >= sh.n_bkv * sh.nsub) return;
-  const int bkv = bucket / sh.nsub, u = bucket - bkv * sh.nsub;
+  if (bucket >= sh.n_bkv * sh.n_win * sh.nsub) return;
+  const int bkv = bucket / (sh.n_win * sh.nsub), u = bucket % sh.nsub;
   const int c = counts[bucket];
   int o = item_off[bucket];
   for (int k = 0; k * sh.item_tokens < c; ++k, ++o)

@@ -777,7 +777,7 @@ int run_host(const nsa_sel_desc* d, const nsa_sel_host_io* io, nsa_stream_t stre
 // ------------------------------------------------------------------ backward
 struct BwdLayout {
   size_t off_delta, off_counts, off_fill, off_tok_off, off_item_off, off_tokens, off_items, total;
-  int n_buckets, nsub, spb, n_blk, G;
+  int n_buckets, nsub, spb, n_blk, G, win_shift, n_win;
   long long max_pairs;
 };
 
@@ -802,13 +802,20 @@ int bwd_layout(const nsa_sel_bwd_desc* d, BwdLayout* L) {
   L->spb = d->block_size / 64;
   L->n_blk = (T + d->block_size - 1) / d->block_size;
   L->nsub = (T + 63) / 64;
+  // Token windows of the inverse index: the Q, dO (bf16) and dQ (fp32) rows of one window, G KB
+  // per token, take 64 MB (half the L2); at most 32 windows per (b, kvh).
+  int ws = G == 16 ? 12 : 13;
+  while (ws < 24 && ((T + (1 << ws) - 1) >> ws) > 32) ++ws;
+  L->win_shift = ws;
+  L->n_win = (T + (1 << ws) - 1) >> ws;
   const long long n_bkv = (long long)B * Hkv;
-  L->n_buckets = (int)(n_bkv * L->nsub);
-  if (n_bkv * L->nsub >= (1ll << 30)) return fail(NSA_ERR_UNSUPPORTED, "too many (b, kvh, sub-block) buckets");
+  const long long nb = n_bkv * L->n_win * L->nsub;
+  if (nb >= (1ll << 30)) return fail(NSA_ERR_UNSUPPORTED, "too many (b, kvh, window, sub-block) buckets");
+  L->n_buckets = (int)nb;
   const long long per_row = std::min<long long>((long long)d->n_sel * L->spb, L->nsub);
   L->max_pairs = n_bkv * T * per_row;
   if (L->max_pairs >= (1ll << 31)) return fail(NSA_ERR_UNSUPPORTED, "selection index exceeds 2^31 entries");
-  const long long max_items = L->max_pairs / nsa::bwd::kItemTokens + L->n_buckets;
+  const long long max_items = L->max_pairs / nsa::bwd::kItemTokens + L->n_buckets;  // ceil per bucket
   size_t o = 0;
   L->off_delta = o; o = align16(o + (size_t)B * Hq * T * 4);
   L->off_counts = o; o = align16(o + (size_t)L->n_buckets * 4);
@@ -850,8 +857,9 @@ int backward(const nsa_sel_bwd_desc* d, nsa_stream_t stream) {
   int32_t* tokens = reinterpret_cast<int32_t*>(ws + L.off_tokens);
   int4* items = reinterpret_cast<int4*>(ws + L.off_items);
 
-  // tensor maps: Q and dO per token (G heads x 64 dims per box), K and V per 64-key sub-block
-  CUtensorMap tmQ, tmDO, tmK, tmV;
+  // tensor maps: Q and dO per token (G heads x 64 dims per box), K and V per 64-key sub-block,
+  // dQ (fp32, reduce-add) per token (G heads x 32 dims per box)
+  CUtensorMap tmQ, tmDO, tmK, tmV, tmDQ;
   {
     const cuuint64_t dims[4] = {128, (cuuint64_t)T, (cuuint64_t)Hq, (cuuint64_t)B};
     const cuuint64_t str[3] = {256, 256ull * T, 256ull * T * Hq};
@@ -861,6 +869,11 @@ int backward(const nsa_sel_bwd_desc* d, nsa_stream_t stream) {
     if (rc == NSA_OK)
       rc = encode(&tmDO, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, d->d_o, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "dO");
+    if (rc != NSA_OK) return rc;
+    const cuuint64_t str32[3] = {512, 512ull * T, 512ull * T * Hq};
+    const cuuint32_t box32[4] = {32, 1, (cuuint32_t)G, 1};
+    rc = encode(&tmDQ, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, d->dq, dims, str32, box32, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "dQ");
     if (rc != NSA_OK) return rc;
   }
   {
@@ -897,7 +910,7 @@ int backward(const nsa_sel_bwd_desc* d, nsa_stream_t stream) {
   // 2. inverse index: counts, offsets, token lists, work items
   e = cudaMemsetAsync(counts, 0, L.off_tok_off - L.off_counts, st);  // counts and fill counters
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(backward index counters)");
-  nsa::bwd::IndexShape sh{B * Hkv, T, d->n_sel, L.spb, L.n_blk, L.nsub, nsa::bwd::kItemTokens};
+  nsa::bwd::IndexShape sh{B * Hkv, T, d->n_sel, L.spb, L.n_blk, L.nsub, nsa::bwd::kItemTokens, L.win_shift, L.n_win};
   const unsigned row_blocks = (unsigned)(((long long)B * Hkv * T + 255) / 256);
   nsa::bwd::index_rows_kernel<false><<<row_blocks, 256, 0, st>>>(d->sel, sh, counts, nullptr, nullptr, nullptr);
   nsa::bwd::index_scan_kernel<<<1, 1024, 0, st>>>(counts, L.n_buckets, nsa::bwd::kItemTokens, tok_off, item_off);
@@ -912,7 +925,6 @@ int backward(const nsa_sel_bwd_desc* d, nsa_stream_t stream) {
   p.items = reinterpret_cast<const int32_t*>(items);
   p.lse = d->lse;
   p.delta = delta;
-  p.dq = d->dq;
   p.dk = d->dk;
   p.dv = d->dv;
   p.err = d->err;
@@ -934,7 +946,7 @@ int backward(const nsa_sel_bwd_desc* d, nsa_stream_t stream) {
   p.timeout_ns = (unsigned long long)tmo * 1000000ull;
   int grid = sm;
   if (d->max_ctas > 0 && d->max_ctas < grid) grid = d->max_ctas;
-  void* args[] = {&tmQ, &tmDO, &tmK, &tmV, &p};
+  void* args[] = {&tmQ, &tmDO, &tmK, &tmV, &tmDQ, &p};
   e = cudaLaunchKernel(reinterpret_cast<const void*>(&nsa::bwd::nsa_bwd_kernel), dim3(grid),
                        dim3(nsa::bwd::kThreads), args, nsa::bwd::kSmemBytes, st);
   if (e != cudaSuccess) return cuda_fail(e, "backward kernel launch");

@@ -205,9 +205,10 @@ def _bwd(**kw):
 
 def test_backward_workspace_bytes():
     """Row sums (B*Hq*T floats) + index: 4 bucket arrays, token entries (B*Hkv*T*KSEL*l'/64 at
-    most) and 16-byte work items, each region 16-byte aligned."""
+    most) and 16-byte work items, each region 16-byte aligned.  A bucket is (b*Hkv + kvh, token
+    window, 64-key sub-block): 4096-token windows for G = 16 at T = 64K."""
     n = capi.backward_workspace_bytes(_bwd())
-    rows, buckets, pairs = 64 * 65536, 4 * 1024, 4 * 65536 * 16
+    rows, buckets, pairs = 64 * 65536, 4 * 16 * 1024, 4 * 65536 * 16
     expect = rows * 4 + 3 * buckets * 4 + (buckets + 1) * 4 + pairs * 4 + (pairs // 128 + buckets) * 16
     assert expect <= n <= expect + 7 * 16
     assert capi.backward_workspace_bytes(_bwd(block_size=128, n_sel=4)) < n
