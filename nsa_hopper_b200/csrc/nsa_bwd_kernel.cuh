@@ -15,8 +15,8 @@
 // sub-block with up to kItemTokens of its tokens.  Items are ordered by window, so the CTAs sweep
 // the tokens of one window at a time and its Q, dO and dQ rows stay in L2.  A CTA loads K_u, V_u
 // once per item (TMA, 16 KB each) and walks the item's tokens in groups of 128 / G (128 query
-// rows), each gathered by TMA (one box of G heads per token and 64-dim slice, issued by one lane
-// per token), with five tcgen05 UMMAs per group:
+// rows), each gathered by TMA (one box of G heads x 128 dims per token and tensor, issued by one
+// lane per token), with five tcgen05 UMMAs per group:
 //     S  [128 rows x 64 keys]  = Q_g  . K_u^T        (A K-major, B K-major)
 //     dP [128 rows x 64 keys]  = dO_g . V_u^T        (A K-major, B K-major)
 //     dV^T [128 d x 64 keys]  += dO_g^T . P          (A MN-major, B MN-major; TMEM accumulator)
@@ -56,12 +56,16 @@ constexpr uint32_t kKVSlice = kKeys * 128;                 // one 64-dim slice o
 constexpr uint32_t kKVTile = 2 * kKVSlice;                 // K_u or V_u: 16 KB
 constexpr uint32_t kRowSlice = kRows * 128;                // one 64-dim slice of a 128-row tile: 16 KB
 constexpr uint32_t kRowTile = 2 * kRowSlice;               // Q_g or dO_g: 32 KB
+// A Q / dO tile holds 8-row groups (rows 8i .. 8i+7 = 8 heads of one token) at 2 KB strides, the
+// two 64-dim slices of a group 1 KB apart: one TMA box fills a token's G heads x 128 dims.
+constexpr uint32_t kGrpStride = 2048, kSliceOff = 1024;
 constexpr uint32_t kOffK = 0, kOffV = kKVTile;
 constexpr uint32_t kOffQ = 2 * kKVTile;                    // [buf][Q, dO]
 constexpr uint32_t kOffP = kOffQ + 4 * kRowTile;           // P [128 rows x 64 keys] bf16, SW128
 constexpr uint32_t kOffDS = kOffP + kRows * 128;           // dS, same layout
-// dQ staging: per softmax-gradient warp, its 32 rows x 64 fp32 dimensions (half of d) as two
-// SW128 [32 rows x 128 B] tiles, the source of the TMA reduce-add into dQ
+// dQ staging: per softmax-gradient warp, its 32 rows x 64 fp32 dimensions (half of d): per token
+// and 8-head octet, [2 x 32-dim chunks][8 heads][128 B] SW128, the source of one TMA reduce-add
+// per token
 constexpr uint32_t kStageWarp = 2 * 32 * 128;              // 8 KB
 constexpr uint32_t kOffStage = kOffDS + kRows * 128;
 constexpr uint32_t kOffBar = kOffStage + 4 * kStageWarp;
@@ -96,15 +100,16 @@ constexpr uint32_t kIdescDQ = ptx::idesc_bf16_f32(128, 128, false, true);
 __device__ __forceinline__ int group_count(int count, int R) { return (count + R - 1) / R; }
 
 // dQ of one group (TMEM buffer `tm_dq`, lane = query row of this warp) into the fp32 dQ: each half
-// of d goes through this warp's staging tiles (scaled, SW128) and one TMA reduce-add per (token,
-// 32 dimensions).  `t` is the token of this lane's row (-1: padding row); rows s*G .. s*G+G-1 of
-// the warp are the G heads of one token.  Releases the TMEM buffer once it has been read.
+// of d goes through this warp's staging tiles (scaled, SW128) and one TMA reduce-add per token.
+// `t` is the token of this lane's row (-1: padding row); rows s*G .. s*G+G-1 of the warp are the
+// G heads of one token.  Releases the TMEM buffer once it has been read.
 __device__ __forceinline__ bool dq_flush(const Waiter& w, Bars* bars, uint32_t j, uint32_t tm_dq, uint8_t* stage,
-                                         const CUtensorMap* tmDQ, int t, int b, int kvh, int G, float scale,
-                                         int lane) {
+                                         const CUtensorMap* tmDQ, int t, int hb0, int G, float scale, int lane) {
   if (!w.wait(&bars->dq_full[j & 1], (j >> 1) & 1)) return false;
   ptx::tc_fence_after();
-  const uint32_t st0 = ptx::smem_u32(stage);
+  // this lane's 128-byte rows: token block (lane / G) * G * 256, octet (lane % G) / 8, head lane % 8
+  const uint32_t row0 = ptx::smem_u32(stage) + (uint32_t)(lane / G) * G * 256 + (uint32_t)((lane % G) >> 3) * 2048 +
+                        (uint32_t)(lane & 7) * 128;
 #pragma unroll 1
   for (int half = 0; half < 2; ++half) {
     float a[32], c[32];
@@ -120,12 +125,12 @@ __device__ __forceinline__ bool dq_flush(const Waiter& w, Bars* bars, uint32_t j
     if (lane == 0) ptx::bulk_wait_read<0>();
     __syncwarp();
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {  // 16-byte chunk k of the row, at SW128 position k ^ (row & 7)
-      const uint32_t off = (uint32_t)lane * 128 + (uint32_t)((k ^ (lane & 7)) << 4);
-      asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(st0 + off), "f"(a[4 * k] * scale),
+    for (int k = 0; k < 8; ++k) {  // 16-byte chunk k of a row, at SW128 position k ^ (head & 7)
+      const uint32_t off = row0 + (uint32_t)((k ^ (lane & 7)) << 4);
+      asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(off), "f"(a[4 * k] * scale),
                    "f"(a[4 * k + 1] * scale), "f"(a[4 * k + 2] * scale), "f"(a[4 * k + 3] * scale)
                    : "memory");
-      asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(st0 + 4096 + off), "f"(c[4 * k] * scale),
+      asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(off + 1024), "f"(c[4 * k] * scale),
                    "f"(c[4 * k + 1] * scale), "f"(c[4 * k + 2] * scale), "f"(c[4 * k + 3] * scale)
                    : "memory");
     }
@@ -133,10 +138,7 @@ __device__ __forceinline__ bool dq_flush(const Waiter& w, Bars* bars, uint32_t j
     __syncwarp();
     for (int s = 0; s < 32 / G; ++s) {
       const int ts = __shfl_sync(0xffffffffu, t, s * G);
-      if (lane == 0 && ts >= 0) {
-        ptx::tma_reduce_add_4d(tmDQ, stage + s * G * 128, half * 64, ts, kvh * G, b);
-        ptx::tma_reduce_add_4d(tmDQ, stage + 4096 + s * G * 128, half * 64 + 32, ts, kvh * G, b);
-      }
+      if (lane == 0 && ts >= 0) ptx::tma_reduce_add_5d(tmDQ, stage + s * G * 256, 0, 0, half * 2, ts, hb0);
     }
     if (lane == 0) ptx::bulk_commit();
   }
@@ -232,14 +234,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) break;
         ++q_issued;
-        if (lane < nt) {
-          uint8_t* qd = smem + kOffQ + buf * 2 * kRowTile;
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            const uint32_t off = c * kRowSlice + (uint32_t)(lane * p.G) * 128;
-            ptx::tma_load_4d(qd + off, &tmQ, &bars->q_full[buf], c * 64, t, kvh * p.G, b, pol_q);
-            ptx::tma_load_4d(qd + kRowTile + off, &tmDO, &bars->q_full[buf], c * 64, t, kvh * p.G, b, pol_q);
-          }
+        if (lane < nt) {  // token `lane`: its G heads x 128 dims, one box per tensor
+          uint8_t* qd = smem + kOffQ + buf * 2 * kRowTile + (uint32_t)(lane * p.G) * 256;
+          const int hb0 = (b * p.Hq + kvh * p.G) >> 3;
+          ptx::tma_load_5d(qd, &tmQ, &bars->q_full[buf], 0, 0, 0, t, hb0, pol_q);
+          ptx::tma_load_5d(qd + kRowTile, &tmDO, &bars->q_full[buf], 0, 0, 0, t, hb0, pol_q);
         }
         __syncwarp();
       }
@@ -274,14 +273,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           ptx::tc_fence_after();
 #pragma unroll
           for (int j = 0; j < kD / 16; ++j) {
-            const uint32_t oa = (j >> 2) * kRowSlice + (j & 3) * 32, ob = (j >> 2) * kKVSlice + (j & 3) * 32;
-            ptx::umma_bf16(tmem + kTmS, ptx::sdesc_sw128(q_base + oa, 16, 1024),
+            const uint32_t oa = (j >> 2) * kSliceOff + (j & 3) * 32, ob = (j >> 2) * kKVSlice + (j & 3) * 32;
+            ptx::umma_bf16(tmem + kTmS, ptx::sdesc_sw128(q_base + oa, 16, kGrpStride),
                            ptx::sdesc_sw128(k_base + ob, 16, 1024), kIdescS, j > 0 ? 1u : 0u);
           }
 #pragma unroll
           for (int j = 0; j < kD / 16; ++j) {
-            const uint32_t oa = (j >> 2) * kRowSlice + (j & 3) * 32, ob = (j >> 2) * kKVSlice + (j & 3) * 32;
-            ptx::umma_bf16(tmem + kTmDP, ptx::sdesc_sw128(do_base + oa, 16, 1024),
+            const uint32_t oa = (j >> 2) * kSliceOff + (j & 3) * 32, ob = (j >> 2) * kKVSlice + (j & 3) * 32;
+            ptx::umma_bf16(tmem + kTmDP, ptx::sdesc_sw128(do_base + oa, 16, kGrpStride),
                            ptx::sdesc_sw128(v_base + ob, 16, 1024), kIdescS, j > 0 ? 1u : 0u);
           }
           ptx::umma_commit(&bars->s_full);
@@ -294,11 +293,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           ptx::tc_fence_after();
 #pragma unroll
           for (int j = 0; j < kRows / 16; ++j) {  // K = query rows, 16 per step
-            const uint32_t o = (uint32_t)j * 2048;
+            const uint32_t o = (uint32_t)j * 2048, oq = (uint32_t)j * 2 * kGrpStride;
             const uint32_t acc = (g > 0 || j > 0) ? 1u : 0u;
-            ptx::umma_bf16(tmem + kTmDV, ptx::sdesc_sw128(do_base + o, kRowSlice, 1024),
+            ptx::umma_bf16(tmem + kTmDV, ptx::sdesc_sw128(do_base + oq, kSliceOff, kGrpStride),
                            ptx::sdesc_sw128(p_base + o, kRowSlice, 1024), kIdescAcc, acc);
-            ptx::umma_bf16(tmem + kTmDK, ptx::sdesc_sw128(q_base + o, kRowSlice, 1024),
+            ptx::umma_bf16(tmem + kTmDK, ptx::sdesc_sw128(q_base + oq, kSliceOff, kGrpStride),
                            ptx::sdesc_sw128(ds_base + o, kRowSlice, 1024), kIdescAcc, acc);
           }
 #pragma unroll
@@ -330,7 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* stage = smem + kOffStage + (uint32_t)quarter * kStageWarp;
     uint32_t m = 0, n = 0;
     bool dead = false;
-    int pend_t = -1, pend_b = 0, pend_kvh = 0;  // the group whose dQ is still in TMEM
+    int pend_t = -1, pend_hb = 0;  // the group whose dQ is still in TMEM: this row's token, first head octet
     uint8_t* prow = smem + kOffP + (uint32_t)r * 128;
     uint8_t* dsrow = smem + kOffDS + (uint32_t)r * 128;
     for (int it = blockIdx.x; it < n_items && !dead; it += gridDim.x, ++m) {
@@ -395,12 +394,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         // dQ of the previous group
         if (n >= 1) {
           dead |= !dq_flush(w, bars, n - 1, tmem + lane_addr + kTmDQ + ((n - 1) & 1) * 128, stage, &tmDQ, pend_t,
-                            pend_b, pend_kvh, p.G, p.scale, lane);
+                            pend_hb, p.G, p.scale, lane);
           if (dead) break;
         }
         pend_t = t;
-        pend_b = b;
-        pend_kvh = kvh;
+        pend_hb = (b * p.Hq + kvh * p.G) >> 3;
       }
       if (dead) break;
       // dK^T, dV^T of the item: lane r = dimension, column j = key key0 + j
@@ -431,8 +429,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     // dQ of the last group
     if (!dead && n >= 1)
-      dq_flush(w, bars, n - 1, tmem + lane_addr + kTmDQ + ((n - 1) & 1) * 128, stage, &tmDQ, pend_t, pend_b,
-               pend_kvh, p.G, p.scale, lane);
+      dq_flush(w, bars, n - 1, tmem + lane_addr + kTmDQ + ((n - 1) & 1) * 128, stage, &tmDQ, pend_t, pend_hb, p.G,
+               p.scale, lane);
     // every reduce has completed before the CTA (and its shared memory) goes away
     if (lane == 0) ptx::bulk_wait<0>();
     __syncwarp();

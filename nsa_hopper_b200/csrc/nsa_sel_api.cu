@@ -857,22 +857,27 @@ int backward(const nsa_sel_bwd_desc* d, nsa_stream_t stream) {
   int32_t* tokens = reinterpret_cast<int32_t*>(ws + L.off_tokens);
   int4* items = reinterpret_cast<int4*>(ws + L.off_items);
 
-  // tensor maps: Q and dO per token (G heads x 64 dims per box), K and V per 64-key sub-block,
-  // dQ (fp32, reduce-add) per token (G heads x 32 dims per box)
+  // Tensor maps.  Q, dO (bf16) and dQ (fp32) are [B, Hq, T, 128]; they are described as 5D views
+  // (dims in element order: dimension-in-chunk, head-in-octet, dimension chunk, token, head octet
+  // of the whole batch) so that one box holds a token's G heads x 128 dims laid out as 8-head
+  // groups, each group's dimension chunks 1 KB apart -- the UMMA operand layout of the kernel.
+  // The strides are not increasing (head before dimension chunk); the hardware only sums
+  // coordinate x stride.  K and V per 64-key sub-block.
   CUtensorMap tmQ, tmDO, tmK, tmV, tmDQ;
   {
-    const cuuint64_t dims[4] = {128, (cuuint64_t)T, (cuuint64_t)Hq, (cuuint64_t)B};
-    const cuuint64_t str[3] = {256, 256ull * T, 256ull * T * Hq};
-    const cuuint32_t box[4] = {64, 1, (cuuint32_t)G, 1};
-    rc = encode(&tmQ, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, d->q, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B,
+    const cuuint64_t dims[5] = {64, 8, 2, (cuuint64_t)T, (cuuint64_t)(Hq / 8) * B};
+    const cuuint64_t str[4] = {256ull * T, 128, 256, 8ull * 256 * T};
+    const cuuint32_t box[5] = {64, 8, 2, 1, (cuuint32_t)(G / 8)};
+    rc = encode(&tmQ, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, d->q, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B,
                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "Q");
     if (rc == NSA_OK)
-      rc = encode(&tmDO, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, d->d_o, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B,
+      rc = encode(&tmDO, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, d->d_o, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "dO");
     if (rc != NSA_OK) return rc;
-    const cuuint64_t str32[3] = {512, 512ull * T, 512ull * T * Hq};
-    const cuuint32_t box32[4] = {32, 1, (cuuint32_t)G, 1};
-    rc = encode(&tmDQ, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, d->dq, dims, str32, box32, CU_TENSOR_MAP_SWIZZLE_128B,
+    const cuuint64_t dims32[5] = {32, 8, 4, (cuuint64_t)T, (cuuint64_t)(Hq / 8) * B};
+    const cuuint64_t str32[4] = {512ull * T, 128, 512, 8ull * 512 * T};
+    const cuuint32_t box32[5] = {32, 8, 2, 1, (cuuint32_t)(G / 8)};  // half of the dimensions
+    rc = encode(&tmDQ, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, d->dq, dims32, str32, box32, CU_TENSOR_MAP_SWIZZLE_128B,
                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "dQ");
     if (rc != NSA_OK) return rc;
   }
