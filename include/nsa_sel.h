@@ -243,9 +243,11 @@ typedef struct nsa_sel_bwd_desc {
   int32_t reserved[5];
 } nsa_sel_bwd_desc;
 
-/* Bytes of the workspace nsa_sel_backward needs for a description (the row sums dO . O and the
-   inverse selection index: about 4 * (B*Hq*T + 2 * B*Hkv*T*KSEL*l_prime/64) bytes), or -1 if
-   the description is invalid (see nsa_sel_last_error()). */
+/* Bytes of the workspace nsa_sel_backward needs for a description, or -1 if the description is
+   invalid (see nsa_sel_last_error()): the row sums dO . O (4 * B*Hq*T bytes) and the inverse
+   selection index, i.e. about 4.2 bytes per (token, selected 64-key sub-block) pair (at most
+   B*Hkv*T*KSEL*l_prime/64 of them) plus 32 bytes per bucket, a bucket being one (b, kvh, token
+   window, sub-block): B*Hkv * ceil(T/64) * (number of windows, at most 32). */
 int64_t nsa_sel_backward_workspace_bytes(const nsa_sel_bwd_desc* desc);
 
 /* Adds dQ, dK, dV for the description on `stream` (six kernel launches and one memset, no
