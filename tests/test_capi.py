@@ -214,6 +214,21 @@ def test_backward_workspace_bytes():
     assert capi.backward_workspace_bytes(_bwd(block_size=128, n_sel=4)) < n
 
 
+@pytest.mark.parametrize("Hq, Hkv, T, n_win", [
+    (64, 8, 65536, 8),      # G = 8: 8192-token windows
+    (64, 4, 4096, 1),       # one window
+    (64, 4, 1 << 20, 32),   # long sequences: at most 32 windows (32768 tokens each)
+    (64, 4, 4097, 2),       # a partial last window
+])
+def test_backward_workspace_counts_token_windows(Hq, Hkv, T, n_win):
+    """The inverse index has one bucket per (b*Hkv + kvh, token window, 64-key sub-block)."""
+    n = capi.backward_workspace_bytes(_bwd(heads_q=Hq, heads_kv=Hkv, seq_len=T, n_sel=4))
+    nsub = (T + 63) // 64
+    rows, buckets, pairs = Hq * T, Hkv * n_win * nsub, Hkv * T * min(4, nsub)
+    expect = rows * 4 + 3 * buckets * 4 + (buckets + 1) * 4 + pairs * 4 + (pairs // 128 + buckets) * 16
+    assert expect <= n <= expect + 7 * 16
+
+
 @pytest.mark.parametrize("kw, code", [
     (dict(heads_q=32, heads_kv=8), capi.NSA_ERR_UNSUPPORTED),   # G = 4
     (dict(d=64), capi.NSA_ERR_UNSUPPORTED),
