@@ -77,13 +77,39 @@ def test_backward_sum_identities_and_dq_window_at_a_larger_size():
         assert scaled_err(dq[0, h, t0:t0 + 128].cpu().numpy(), r) <= GRAD_TOL
 
 
+def test_backward_group8_lp128_across_token_windows():
+    """G = 8 (one 8-head octet per token box, 8192-token windows) with l' = 128 blocks on a
+    sequence of three windows, the last one partial: the exact sum identities on everything and
+    dQ windows in each token window against the restatement."""
+    B, Hq, Hkv, T, D, n, lp = 1, 32, 4, 2 * 8192 + 100, 128, 8, 128
+    q, k, v = make_qkv(B, Hq, Hkv, T, D, D, 45)
+    g = torch.Generator().manual_seed(46)
+    d_o = torch.randn(B, Hq, T, D, generator=g).to(torch.bfloat16)
+    sel = indices.rule0(B, Hkv, T, n, lp, seed=45)
+    o, lse = _forward(q, k, v, sel, lp)
+    dq, dk, dv, err = run_backward_capi(q, k, v, sel, d_o, o, lse, l_prime=lp)
+    assert int(err.item()) == 0
+    G = Hq // Hkv
+    sum_do = d_o.double().view(B, Hkv, G, T, D).sum((2, 3))
+    scale_dv = d_o.double().abs().view(B, Hkv, G, T, D).sum((2, 3))
+    assert ((dv.double().cpu().sum(2) - sum_do).abs() <= 5e-3 * scale_dv + 1e-2).all()
+    assert (dk.double().cpu().sum(2).abs() <= 5e-3 * dk.double().cpu().abs().sum(2) + 1e-2).all()
+    for h, t0 in ((3, 4000), (17, 8192 + 77), (30, T - 64)):
+        r = obwd.dq_rows(q, k, v, sel, lp, d_o, 0, h, t0, t0 + 64)
+        assert scaled_err(dq[0, h, t0:t0 + 64].cpu().numpy(), r) <= GRAD_TOL
+
+
 def test_backward_accumulates_into_given_buffers():
+    """A second call adds its gradients to the first call's.  The kernel sums with reductions in
+    an order that changes from run to run (the inverse index is filled by atomic counters), so
+    the second call's own gradients differ from the first's in the last bits: the bound is 1e-4
+    of each tensor's largest magnitude (fp32 sums of a few hundred terms differ by far less)."""
     c = golden_cases.load_bwd("bwd_rule0_g16")
     o, lse = _forward(c["q"], c["k"], c["v"], c["sel"], c["LP"])
     g1 = run_backward_capi(c["q"], c["k"], c["v"], c["sel"], c["d_o"], o, lse)[:3]
     g2 = run_backward_capi(c["q"], c["k"], c["v"], c["sel"], c["d_o"], o, lse, grads=tuple(x.clone() for x in g1))[:3]
     for a, b in zip(g1, g2):
-        torch.testing.assert_close(b, 2 * a, rtol=1e-5, atol=1e-5)
+        torch.testing.assert_close(b, 2 * a, rtol=1e-4, atol=1e-4 * float(a.abs().max()))
 
 
 def test_autograd_function_gives_the_kernel_gradients():
