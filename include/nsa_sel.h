@@ -1,5 +1,6 @@
 /*
- * nsa_sel.h -- C ABI of the B200 (sm_100a) NSA selected-branch attention forward.
+ * nsa_sel.h -- C ABI of the B200 (sm_100a) NSA selected-branch attention forward, with the
+ * block selection that produces its index rows and the backward that the reference lacks.
  *
  * This is the drop-in boundary for the one hot path of the nsa-hopper reference: the
  * selected-branch forward that its kernels expose through pybind as
