@@ -253,3 +253,19 @@ def test_backward_rejects_null_and_misaligned_pointers_before_touching_a_device(
     with pytest.raises(capi.NsaSelError) as ei:
         capi.backward(_bwd(dk=24))
     assert ei.value.code == capi.NSA_ERR_INVALID_ARG
+
+
+def test_torch_backward_checks_its_tensors_before_any_device_call():
+    """ops.backward refuses host tensors and wrong dtypes with a ValueError (no GPU needed)."""
+    import torch
+
+    from nsa_hopper_b200 import ops
+
+    q = torch.zeros(1, 16, 64, 128, dtype=torch.bfloat16)
+    k = torch.zeros(1, 2, 64, 128, dtype=torch.bfloat16)
+    sel = torch.zeros(1, 2, 64, 1, dtype=torch.int32)
+    lse = torch.zeros(1, 16, 64)
+    with pytest.raises(ValueError, match="Q must be a contiguous bf16 CUDA tensor"):
+        ops.backward(q, k, k, sel, q, lse, q)
+    with pytest.raises(ValueError, match="Q must be"):
+        ops.backward(q.float(), k, k, sel, q, lse, q)
